@@ -1,0 +1,429 @@
+#!/usr/bin/env python
+"""Benchmark of the four-op hot path on B200; prints ONE JSON line (rank 0).
+
+Headline workload (N=1): swiglu at the Llama-3-8B MLP shape, x [4096, 4096], w1/w3
+[4096, 14336] fp16 (seed 1), metric TFLOP/s = 4*M*N*K / time. With N GPUs (torchrun, one
+process per GPU) the same problem is column-sharded over N (each rank computes
+out[:, N/g slice]) and the output is all-gathered over NVLink with NCCL (strong scaling).
+At N=1 the line also carries the other three operators at their configurations under
+"ops" (rmsnorm_rope, flash_attention causal/non-causal, paged_attention decode).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the CPU oracle (a numpy restatement of the reference's
+python/triton_llm/reference/swiglu.py) on the host cores on a bounded row sample of the same
+workload; under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from datetime import timedelta
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+SWIGLU_SHAPE = (4096, 4096, 14336)  # M, K, N
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-ops", action="store_true", help="skip the per-operator extras")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {k: float(p[k]) for k in FALLBACK_PEAKS}, "measured"
+    except Exception:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profile_traffic(name: str):
+    """Bytes per launch recorded in a committed ncu summary (line 'traffic_bytes_per_launch: N')."""
+    path = os.path.join(ROOT, "profiles", name)
+    try:
+        for line in open(path):
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        finally:
+            os.unlink(self.path)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------
+def _events_time(torch, fn, steps, warmup, flush=None):
+    """Runs fn() warmup+steps times; returns per-step device milliseconds (CUDA events on the
+    current stream), flushing L2 between timed steps when `flush` is given."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    st = torch.cuda.current_stream()
+    for _ in range(steps):
+        if flush is not None:
+            flush.zero_()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        fn()
+        b.record(st)
+        times.append((a, b))
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in times]
+
+
+def _cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
+        if n:
+            return max(n)
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def cpu_swiglu_inputs(rows=512):
+    """A row sample of the swiglu workload for the CPU oracle (fp16-representable fp32)."""
+    import numpy as np
+
+    from oracle import ops_oracle as O
+
+    M, K, N = SWIGLU_SHAPE
+    rng = np.random.default_rng(1)
+    x = O.round_to(rng.standard_normal((rows, K), dtype=np.float32), "fp16")
+    w1 = O.round_to(rng.standard_normal((K, N), dtype=np.float32) / np.float32(math.sqrt(K)), "fp16")
+    w3 = O.round_to(rng.standard_normal((K, N), dtype=np.float32) / np.float32(math.sqrt(K)), "fp16")
+    return x, w1, w3
+
+
+def cpu_swiglu_baseline(inputs=None, min_seconds=8.0, rows=512):
+    """Times the numpy oracle on a bounded row sample of the swiglu workload (all host cores)."""
+    from oracle import ops_oracle as O
+
+    M, K, N = SWIGLU_SHAPE
+    x, w1, w3 = inputs if inputs is not None else cpu_swiglu_inputs(rows)
+    x = x[:rows]
+    O.swiglu(x[:16], w1, w3)  # warm the BLAS thread pool
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        O.swiglu(x, w1, w3)
+        reps += 1
+        el = time.perf_counter() - t0
+        if (el >= min_seconds and reps >= 2) or reps >= 50:
+            break
+    flops = 4.0 * x.shape[0] * K * N * reps
+    return {"value": flops / el / 1e12, "unit": "TFLOP/s", "cores": _cpu_threads(), "kind": "port",
+            "sample": f"{reps} x numpy-oracle swiglu on {x.shape[0]} of {M} rows (K={K}, N={N}), "
+                      f"{el:.1f} s"}
+
+
+# ------------------------------------------------------------------------------------------
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    M, K, N = SWIGLU_SHAPE
+    inputs = cpu_swiglu_inputs(256)
+    vals, cores = [], 1
+    for i in range(args.warmup + args.steps):
+        b = cpu_swiglu_baseline(inputs, min_seconds=0.0, rows=256)
+        cores = b["cores"]
+        if i >= args.warmup:
+            vals.append(b["value"])
+    v = statistics.median(vals)
+    ms = 4.0 * M * K * N / (v * 1e12) * 1e3
+    line = {
+        "impl": "reference", "metric": "swiglu TFLOP/s", "value": v, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+        "data": "synthetic (seeded normal, x~N(0,1), w~N(0,1/K))",
+        "config": {"workload": f"swiglu M{M} K{K} N{N} fp16 (Llama-3-8B MLP)",
+                   "note": "CPU oracle (numpy restatement of reference/swiglu.py); each step is a "
+                           "256-row sample, extrapolated to the full workload"},
+        "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "sample": "256-row samples of the swiglu workload per step"},
+        "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------
+def extra_ops(torch, T, peaks):
+    """The other three operators at their configurations (N=1, rank 0)."""
+    res = {}
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    hbm = peaks["hbm_gbs"]
+    tc = peaks["bf16_tflops"]
+
+    def gen(shape, seed, scale=1.0):
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        return (torch.randn(shape, generator=g, device="cuda") * scale).half()
+
+    # rmsnorm_rope: config [2,128,8,64] and a bandwidth-scale variant [16,4096,32,128].
+    for name, (b, s, h, d) in [("rmsnorm_rope_cfg_2x128x8x64", (2, 128, 8, 64)),
+                               ("rmsnorm_rope_bw_16x4096x32x128", (16, 4096, 32, 128))]:
+        x = gen((b, s, h, d), 0)
+        w = (1 + 0.1 * torch.randn(d, device="cuda")).half()
+        pos = torch.arange(s, device="cuda", dtype=torch.float32)
+        inv = 1.0 / (10000 ** (torch.arange(0, d, 2, device="cuda").float() / d))
+        emb = torch.cat([torch.outer(pos, inv)] * 2, dim=-1)
+        cos, sin = emb.cos().half(), emb.sin().half()
+        nbytes = 2 * (b * s * h * d * 2) + d * 2 + 2 * (s * d * 2)
+        ts = _events_time(torch, lambda: T.rmsnorm_rope(x, w, cos, sin), 20, 5, flush)
+        t = statistics.median(ts)
+        gbs = nbytes / (t * 1e-3) / 1e9
+        res[name] = {"value": gbs, "unit": "GB/s", "ms": t, "bytes": nbytes,
+                     "roofline_frac": gbs / hbm, "bound": "hbm", "l2": "flushed"}
+        del x
+    # flash_attention: causal [4,32,4096,128] and non-causal [4,32,1024,128].
+    for name, (b, h, s, d), causal in [("flash_causal_4x32x4096x128", (4, 32, 4096, 128), True),
+                                       ("flash_full_4x32x1024x128", (4, 32, 1024, 128), False)]:
+        q, k, v = gen((b, h, s, d), 2), gen((b, h, s, d), 3), gen((b, h, s, d), 4)
+        flops = 4.0 * b * h * s * s * d * (0.5 if causal else 1.0)
+        ts = _events_time(torch, lambda: T.flash_attention(q, k, v, causal=causal), 10, 3, flush)
+        t = statistics.median(ts)
+        tf = flops / (t * 1e-3) / 1e12
+        res[name] = {"value": tf, "unit": "TFLOP/s", "ms": t, "flops": flops,
+                     "roofline_frac": tf / tc, "bound": "tensor"}
+        del q, k, v
+    # paged_attention decode: B64 H32 D128 bs16, lens U[512,8192] (seed 3).
+    g = torch.Generator().manual_seed(3)
+    lens = torch.randint(512, 8193, (64,), dtype=torch.int32, generator=g)
+    nb = [(int(n) + 15) // 16 for n in lens]
+    pool = sum(nb)
+    perm = torch.randperm(pool, generator=g)
+    bt = torch.zeros(64, max(nb), dtype=torch.int32)
+    pos = 0
+    for i, n in enumerate(nb):
+        bt[i, :n] = perm[pos:pos + n].to(torch.int32)
+        pos += n
+    kc, vc = gen((pool, 16, 32, 128), 5), gen((pool, 16, 32, 128), 6)
+    qd = gen((64, 32, 1, 128), 7)
+    btd, cl = bt.cuda(), lens.cuda()
+    nbytes = int(lens.sum()) * 32 * 128 * 2 * 2 + 2 * 64 * 32 * 128 * 2 + sum(nb) * 4 + 64 * 4
+    ts = _events_time(torch, lambda: T.paged_attention(qd, kc, vc, btd, cl, block_size=16), 20, 5, flush)
+    t = statistics.median(ts)
+    gbs = nbytes / (t * 1e-3) / 1e9
+    res["paged_decode_b64_h32_d128_bs16"] = {"value": gbs, "unit": "GB/s", "ms": t, "bytes": nbytes,
+                                              "roofline_frac": gbs / hbm, "bound": "hbm",
+                                              "kv_tokens": int(lens.sum())}
+    del kc, vc
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import tritonllmcompiler_b200 as T
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    peaks, peak_src = load_peaks()
+    M, K, N = SWIGLU_SHAPE
+    assert N % world == 0 and (N // world) % 8 == 0
+    n_loc = N // world
+    g = torch.Generator(device="cuda").manual_seed(1)
+    x = torch.randn(M, K, generator=g, device="cuda").half()
+    w1 = (torch.randn(K, N, generator=g, device="cuda") / math.sqrt(K)).half()
+    w3 = (torch.randn(K, N, generator=g, device="cuda") / math.sqrt(K)).half()
+    w1l = w1[:, rank * n_loc:(rank + 1) * n_loc].contiguous()
+    w3l = w3[:, rank * n_loc:(rank + 1) * n_loc].contiguous()
+    del w1, w3
+    gathered = torch.empty(world * M * n_loc, dtype=torch.float16, device="cuda") if world > 1 else None
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+
+    def kernel_only():
+        return T.swiglu(x, w1l, w3l)
+
+    def step():
+        out = T.swiglu(x, w1l, w3l)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out)
+            out = gathered.view(world, M, n_loc).permute(1, 0, 2).reshape(M, N)
+        return out
+
+    flops = 4.0 * M * K * N
+    # Warm-up (also JIT-free: the library is prebuilt).
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        times = _events_time(torch, step, args.steps, 0, flush)
+    torch.cuda.synchronize()
+    t_step = sum(times) / len(times)
+    if world > 1:
+        tt = torch.tensor([t_step], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_step = float(tt.item())
+        dist.barrier()
+    value = flops / (t_step * 1e-3) / 1e12
+
+    # Kernel-only roofline: the swiglu kernel alone, CUDA events on its launch stream.
+    kt = _events_time(torch, kernel_only, max(5, args.steps // 2), 2, flush)
+    k_ms = sum(kt) / len(kt)
+    k_flops = 4.0 * M * K * n_loc
+    achieved = k_flops / (k_ms * 1e-3) / 1e12
+    traffic = profile_traffic("swiglu_m4096_k4096_n14336_fp16.md") if world == 1 else None
+
+    # End to end through the public API with pinned host buffers (H2D inputs, D2H result).
+    hx = x.cpu().pin_memory()
+    h1 = w1l.cpu().pin_memory()
+    h3 = w3l.cpu().pin_memory()
+    hout = torch.empty((M, n_loc), dtype=torch.float16).pin_memory()
+    dx, d1, d3 = torch.empty_like(x), torch.empty_like(w1l), torch.empty_like(w3l)
+
+    def e2e_step():
+        dx.copy_(hx, non_blocking=True)
+        d1.copy_(h1, non_blocking=True)
+        d3.copy_(h3, non_blocking=True)
+        out = T.swiglu(dx, d1, d3)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out)
+        hout.copy_(out, non_blocking=True)
+
+    et = _events_time(torch, e2e_step, max(3, args.steps // 4), 2)
+    e_ms = sum(et) / len(et)
+    if world > 1:
+        tt = torch.tensor([e_ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e_ms = float(tt.item())
+    e2e = {"value": flops / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+           "h2d_bytes_per_step": (hx.numel() + h1.numel() + h3.numel()) * 2,
+           "d2h_bytes_per_step": hout.numel() * 2, "ms_per_step": e_ms}
+
+    ops = None
+    cpu = None
+    if rank == 0 and world == 1:
+        if not args.no_ops:
+            del dx, d1, d3
+            torch.cuda.empty_cache()
+            ops = extra_ops(torch, T, peaks)
+        if not args.no_cpu:
+            cpu = cpu_swiglu_baseline()
+
+    if rank == 0:
+        peak = peaks["bf16_tflops"]
+        line = {
+            "metric": "swiglu TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic (seeded normal, x~N(0,1), w~N(0,1/K))",
+            "config": {"workload": f"swiglu M{M} K{K} N{N} fp16 (Llama-3-8B MLP)",
+                       "parallelism": "single GPU" if world == 1 else
+                       f"column-shard N over {world} ranks + NCCL all_gather_into_tensor + permute",
+                       "l2": "256 MiB buffer written between timed steps; inputs 267 MB > L2"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": f"{peak_src} bf16_tflops (dense, burst)",
+                         "kernel_ms": k_ms, "kernel": "swiglu_tc_kernel"},
+            "e2e": e2e,
+            "gpu_launches": args.steps,
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        if ops is not None:
+            line["ops"] = ops
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,128 @@
+/*
+ * tllm_sm100.h -- C ABI of libtllm_sm100a.so, the B200 (sm_100a) implementation of the
+ * four operators exported by triton_llm.ops (xdlhzdh/TritonLLMCompiler).
+ *
+ * Conventions (modelled on mlir/runtime/cutlass_c_api.h:4-25 of the reference: extern "C",
+ * int status with 0 = success, int64_t sizes), extended for a device-pointer hot path:
+ *   - every tensor pointer is a DEVICE pointer to fp16 or bf16 data (dtype: 0 = fp16,
+ *     1 = bf16); indices (block tables, context lengths) are int32 device pointers;
+ *   - strides are in ELEMENTS, innermost dimension last, exactly as torch reports them;
+ *   - work is enqueued on `stream` (a cudaStream_t); no entry point allocates, frees or
+ *     synchronises the device;
+ *   - a non-zero return means nothing was launched; tllm_last_error() then describes why
+ *     (thread-local string, valid until the next call on the same thread).
+ * The Python package (tritonllmcompiler_b200.ops) is the only caller in this repository;
+ * it maps a non-zero status to RuntimeError(tllm_last_error()).
+ */
+#ifndef TLLM_SM100_H_
+#define TLLM_SM100_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TLLM_API __attribute__((visibility("default")))
+#else
+#define TLLM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TLLM_OK 0
+#define TLLM_ERR_INVALID 1   /* bad shape, stride, dtype or alignment */
+#define TLLM_ERR_CUDA 2      /* a CUDA runtime / driver call failed */
+#define TLLM_ERR_WORKSPACE 3 /* workspace pointer null or too small */
+
+#define TLLM_DTYPE_F16 0
+#define TLLM_DTYPE_BF16 1
+
+/* Library version string ("0.2.0", the reference package's __version__). */
+TLLM_API const char *tllm_version(void);
+
+/* Human-readable description of the last failure on the calling thread ("" if none). */
+TLLM_API const char *tllm_last_error(void);
+
+/* Reads and clears the device-side error word of the current device: 0 = no kernel has
+ * reported a problem; otherwise a TLLM_DEV_* code from a bounded wait that gave up.
+ * Synchronises the current device (a debugging aid, not part of the hot path). */
+TLLM_API int tllm_debug_status(int *out);
+
+/*
+ * FlashAttention forward: o = softmax(q k^T * sm_scale [+ causal mask]) v per (b, h).
+ * Replaces flash_attention() in python/triton_llm/ops/flash_attention.py:107-133 and its
+ * Triton kernel _flash_attn_fwd (:17-104). The causal mask is top-left aligned: query row i
+ * sees key columns j <= i (:74-79). q is [B,H,Sq,D], k/v are [B,H,Sk,D] with strides
+ * sq/sk/sv (4 entries each, elements), o is [B,H,Sq,D] with strides so. D in {16,32,64,128}.
+ * The innermost stride must be 1 and the other strides multiples of 8 elements (16 bytes).
+ */
+TLLM_API int tllm_flash_attn_fwd(const void *q, const void *k, const void *v, void *o,
+                        int64_t B, int64_t H, int64_t Sq, int64_t Sk, int64_t D,
+                        const int64_t *sq, const int64_t *sk, const int64_t *sv,
+                        const int64_t *so, float sm_scale, int causal, int dtype,
+                        void *stream);
+
+/*
+ * Bytes of device workspace tllm_paged_attn_decode needs for this problem (the split-KV
+ * partial results). Replaces nothing in the reference (its kernel runs one CTA per (b, h)
+ * and needs none); the Python wrapper allocates this from the torch caching allocator.
+ */
+TLLM_API size_t tllm_paged_attn_workspace_size(int64_t B, int64_t H, int64_t D,
+                                      int64_t block_size, int64_t max_blocks);
+
+/*
+ * Paged-KV decode attention: for each (b, h), attention of the single query q[b,h,0,:]
+ * over tokens 0..context_lens[b]-1, token t living at
+ * k_cache[block_tables[b, t / block_size], t % block_size, h, :] (same for v_cache).
+ * Replaces paged_attention() in python/triton_llm/ops/paged_attention.py:92-128 and its
+ * kernel _paged_attn_kernel (:11-89). Like that kernel, at most max_blocks table entries of
+ * a row are read (tokens past max_blocks * block_size are ignored) and a context length of
+ * 0 yields NaN. Unlike it, no host synchronisation happens (the reference reads
+ * context_lens.max() on the host, :113).
+ *   q [B,H,1,D] strides sq (4), caches [num_blocks, block_size, H, D] strides skc/svc (4),
+ *   block_tables [B, max_blocks] strides sbt (2), context_lens [B] contiguous,
+ *   o [B,H,1,D] strides so (4). D in {16,32,64,128}; block_size in {16,32,64}.
+ * workspace must hold tllm_paged_attn_workspace_size(...) bytes, 256-byte aligned.
+ */
+TLLM_API int tllm_paged_attn_decode(const void *q, const void *k_cache, const void *v_cache,
+                           const int32_t *block_tables, const int32_t *context_lens,
+                           void *o, void *workspace, size_t workspace_bytes,
+                           int64_t B, int64_t H, int64_t D, int64_t block_size,
+                           int64_t max_blocks, int64_t num_blocks,
+                           const int64_t *sq, const int64_t *skc, const int64_t *svc,
+                           const int64_t *sbt, const int64_t *so, float sm_scale,
+                           int dtype, void *stream);
+
+/*
+ * Fused RMSNorm + rotate-half RoPE:
+ *   r = rsqrt(mean(x^2) + eps); y = round_to_dtype(x * r * w);
+ *   out[:D/2] = y1*cos[:D/2] - y2*sin[:D/2]; out[D/2:] = y2*cos[D/2:] + y1*sin[D/2:]
+ * with cos/sin indexed by the sequence position s. Replaces rmsnorm_rope() in
+ * python/triton_llm/ops/rmsnorm_rope.py:51-75 (kernel :9-48). The intermediate rounding of
+ * y to the I/O dtype follows the reference's oracle (python/triton_llm/reference/
+ * norm_rope.py:12-15). x/out [B,S,H,D] strides sx/so (4), w [D] stride sw, cos/sin [S,D]
+ * strides scos/ssin (2). D in {16,32,64,128}.
+ */
+TLLM_API int tllm_rmsnorm_rope(const void *x, const void *w, const void *cos, const void *sin,
+                      void *out, int64_t B, int64_t S, int64_t H, int64_t D,
+                      const int64_t *sx, int64_t sw, const int64_t *scos,
+                      const int64_t *ssin, const int64_t *so, float eps, int dtype,
+                      void *stream);
+
+/*
+ * SwiGLU dual GEMM: out = silu(x @ w1) * (x @ w3), fp32 accumulation, one store in the
+ * I/O dtype. Replaces swiglu() in python/triton_llm/ops/swiglu.py:54-76 (kernel :11-51)
+ * and the fp32 C-ABI cutlass_gemm_swiglu / cutlass_gemm_swiglu_sm90 of
+ * mlir/runtime/cutlass_c_api.h:10-18. x [M,K] row stride lda, w1/w3 [K,N] row strides
+ * ldb1/ldb3, out [M,N] row stride ldo (all elements; inner strides are 1).
+ */
+TLLM_API int tllm_swiglu(const void *x, const void *w1, const void *w3, void *out, int64_t M,
+                int64_t N, int64_t K, int64_t lda, int64_t ldb1, int64_t ldb3,
+                int64_t ldo, int dtype, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TLLM_SM100_H_ */

@@ -1,0 +1,101 @@
+"""ctypes binding of ``libtllm_sm100a.so`` (the C ABI declared in ``include/tllm_sm100.h``).
+
+The library is built in-tree (``python -m tritonllmcompiler_b200.build``). There is no
+fallback: when the library is missing or fails to load, every operator raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libtllm_sm100a.so")
+
+DTYPE_CODES = {torch.float16: 0, torch.bfloat16: 1}
+
+_c_i64p = ctypes.POINTER(ctypes.c_int64)
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+
+# name -> (restype, argtypes); mirrors include/tllm_sm100.h.
+SIGNATURES = {
+    "tllm_version": (ctypes.c_char_p, []),
+    "tllm_last_error": (ctypes.c_char_p, []),
+    "tllm_debug_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "tllm_flash_attn_fwd": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _c_i64p, _c_i64p, _c_i64p, _c_i64p,
+         ctypes.c_float, ctypes.c_int, ctypes.c_int, _vp],
+    ),
+    "tllm_paged_attn_workspace_size": (ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64]),
+    "tllm_paged_attn_decode": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _i64, _i64, _i64, _i64, _i64, _i64,
+         _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, ctypes.c_float, ctypes.c_int, _vp],
+    ),
+    "tllm_rmsnorm_rope": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _c_i64p, _i64, _c_i64p, _c_i64p,
+         _c_i64p, ctypes.c_float, ctypes.c_int, _vp],
+    ),
+    "tllm_swiglu": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_int, _vp],
+    ),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """Loads (once) and returns the extension; raises RuntimeError if it is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"{LIB_PATH} is missing: build it with `python -m tritonllmcompiler_b200.build`"
+                    " (the operators have no non-CUDA implementation)"
+                )
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def check(rc: int) -> None:
+    """Raises RuntimeError with the library's message for a non-zero status."""
+    if rc != 0:
+        msg = load().tllm_last_error().decode("utf-8", "replace")
+        raise RuntimeError(f"libtllm_sm100a: {msg} (status {rc})")
+
+
+def strides(t: torch.Tensor, n: int | None = None):
+    """Element strides of ``t`` as a ctypes int64 array."""
+    s = t.stride()
+    if n is not None:
+        s = tuple(s[:n])
+    return (ctypes.c_int64 * len(s))(*s)
+
+
+def ptr(t: torch.Tensor) -> int:
+    return t.data_ptr()
+
+
+def stream_of(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def debug_status() -> int:
+    """Reads and clears the device error word (synchronises the current device)."""
+    out = ctypes.c_int(0)
+    check(load().tllm_debug_status(ctypes.byref(out)))
+    return out.value

@@ -1,0 +1,122 @@
+// Status plumbing, device attribute cache and TMA descriptor encoding for libtllm_sm100a.so.
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "common.h"
+
+namespace tllm {
+
+namespace {
+thread_local char t_last_error[512] = {0};
+
+std::mutex g_attr_mutex;
+int g_sm_count[64] = {0};
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+cudaError_t g_encode_status = cudaSuccess;
+}  // namespace
+
+int fail(int code, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+void clear_error() { t_last_error[0] = 0; }
+
+int cuda_status(cudaError_t err, const char *what) {
+  if (err == cudaSuccess) return TLLM_OK;
+  return fail(TLLM_ERR_CUDA, "%s failed: %s (%s)", what, cudaGetErrorName(err),
+              cudaGetErrorString(err));
+}
+
+int current_device() {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    cuda_status(e, "cudaGetDevice");
+    return -1;
+  }
+  return dev;
+}
+
+int sm_count() {
+  int dev = current_device();
+  if (dev < 0 || dev >= 64) return 0;
+  std::lock_guard<std::mutex> lock(g_attr_mutex);
+  if (g_sm_count[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    g_sm_count[dev] = n;
+  }
+  return g_sm_count[dev];
+}
+
+int encode_tiled(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t rank, void *base,
+                 const uint64_t *dims, const uint64_t *strides_bytes, const uint32_t *box,
+                 CUtensorMapSwizzle swizzle) {
+  std::call_once(g_encode_once, [] {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    g_encode_status = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (g_encode_status == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!g_encode) {
+    if (g_encode_status != cudaSuccess)
+      return cuda_status(g_encode_status, "cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)");
+    return fail(TLLM_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  }
+  cuuint32_t elem_strides[5] = {1, 1, 1, 1, 1};
+  CUresult r = g_encode(map, dtype, rank, base, reinterpret_cast<const cuuint64_t *>(dims),
+                        reinterpret_cast<const cuuint64_t *>(strides_bytes),
+                        reinterpret_cast<const cuuint32_t *>(box), elem_strides,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(TLLM_ERR_INVALID, "cuTensorMapEncodeTiled failed (CUresult %d, rank %u)",
+                static_cast<int>(r), rank);
+  return TLLM_OK;
+}
+
+// Per-translation-unit device status readers (defined next to each kernel family).
+int flash_read_status(int *out);
+int swiglu_read_status(int *out);
+namespace paged {
+int read_status(int *out);
+}
+
+int read_and_clear_device_status(int *out) {
+  int (*readers[])(int *) = {flash_read_status, swiglu_read_status, paged::read_status};
+  int first = 0;
+  for (auto rd : readers) {
+    int v = 0;
+    int rc = rd(&v);
+    if (rc) return rc;
+    if (!first) first = v;
+  }
+  *out = first;
+  return TLLM_OK;
+}
+
+}  // namespace tllm
+
+extern "C" {
+
+const char *tllm_version(void) { return "0.2.0"; }
+
+const char *tllm_last_error(void) { return tllm::t_last_error; }
+
+int tllm_debug_status(int *out) {
+  if (!out) return tllm::fail(TLLM_ERR_INVALID, "tllm_debug_status: out is null");
+  tllm::clear_error();
+  return tllm::read_and_clear_device_status(out);
+}
+
+}  // extern "C"

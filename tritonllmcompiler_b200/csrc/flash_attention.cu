@@ -1,0 +1,476 @@
+// FlashAttention forward for sm_100a (tcgen05 + TMEM + TMA).
+//
+// Reference: python/triton_llm/ops/flash_attention.py:17-133 (Triton FA-2, 64x64 tiles,
+// online softmax, causal mask applied to every tile with no tile skipping) and the oracle
+// python/triton_llm/reference/flash_attention.py:12-29 (fp32 scores, triu(1) -> -inf mask,
+// softmax, P@V, cast to q.dtype).
+//
+// B200 design: one CTA per (128-row query tile, b, h); grid ordered so the heaviest causal
+// query tiles start first.
+//   warp 0      TMA producer: Q once, then K_j / V_j tiles [128 x D] through two 2-slot rings.
+//   warp 1      allocates 512 TMEM columns; one lane issues the UMMAs:
+//                 S_j = Q K_j^T  (128x128, fp32, TMEM columns [0,128) / [128,256) alternately)
+//                 O  += P_j V_j  (128xD, fp32, TMEM columns [256, 256+D))
+//   warps 2-5   softmax: each thread owns one query row (TMEM lane), reads its S row with
+//               tcgen05.ld, applies scale and mask in fp32 (log2 domain), keeps the running
+//               max/sum in registers, writes P_j (I/O dtype) to shared memory in the UMMA
+//               K-major 128B-swizzle layout and rescales its O row in TMEM when the max grows.
+// Causal: only key tiles j <= i are visited for query tile i; only the diagonal tile and a
+// ragged key tail are masked. The mask is top-left aligned (key j visible to query i iff
+// j <= i), exactly as the reference's offs_m >= offs_n.
+// No TMA multicast is used anywhere. Every mbarrier wait is bounded.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <type_traits>
+
+#include "common.h"
+#include "ptx.cuh"
+
+namespace tllm {
+
+__device__ int g_flash_status = 0;
+
+int flash_read_status(int *out) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_flash_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_status(e, "cudaMemcpyFromSymbol(flash status)");
+  const int zero = 0;
+  e = cudaMemcpyToSymbol(g_flash_status, &zero, sizeof(int));
+  if (e != cudaSuccess) return cuda_status(e, "cudaMemcpyToSymbol(flash status)");
+  *out = v;
+  return TLLM_OK;
+}
+
+namespace flash {
+namespace {
+
+constexpr int BM = 128;  // query rows per CTA
+constexpr int BN = 128;  // key rows per tile
+constexpr int kThreads = 192;
+constexpr int kSoftmaxThreads = 128;
+constexpr int TMEM_COLS = 512;
+constexpr int S_COL0 = 0;
+constexpr int O_COL = 256;
+constexpr float kLog2e = 1.4426950408889634f;
+
+enum : int {
+  SITE_Q = 1,
+  SITE_KFULL = 2,
+  SITE_KEMPTY = 3,
+  SITE_VFULL = 4,
+  SITE_VEMPTY = 5,
+  SITE_SFULL = 6,
+  SITE_PREADY = 7,
+  SITE_PVDONE = 8,
+};
+
+// Shared-memory geometry for head dim D: rows of SWB bytes (the swizzle span), D*2/SWB chunks.
+template <int D>
+struct Geo {
+  static constexpr int SWB = D * 2 >= 128 ? 128 : D * 2;
+  static constexpr int CHUNKS = D * 2 / SWB;
+  static constexpr int CHUNK_BYTES = BM * SWB;  // 128 rows of one swizzle span
+  static constexpr int TILE_BYTES = BM * D * 2;
+  static constexpr uint32_t LAYOUT = SWB == 128 ? 2u : (SWB == 64 ? 4u : 6u);
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_OFF + TILE_BYTES;
+  static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;
+  static constexpr int P_OFF = V_OFF + 2 * TILE_BYTES;
+  static constexpr int P_BYTES = BM * BN * 2;
+  static constexpr int BAR_OFF = P_OFF + P_BYTES;
+  static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+};
+
+struct Args {
+  void *o;
+  int64_t so0, so1, so2, so3;
+  int H, Sq, Sk;
+  int n_qtiles;
+  float scale_log2;
+  int causal;
+  int vec_store;
+};
+
+// K-major operand (Q or K): k16 step `k` of the D reduction.
+template <int D>
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int k) {
+  using G = Geo<D>;
+  const int byte = k * 32;
+  const uint32_t addr = base + (byte / G::SWB) * G::CHUNK_BYTES + (byte % G::SWB);
+  return make_sdesc(addr, 16, 8 * G::SWB, G::LAYOUT);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
+                     const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v, const Args a) {
+  using G = Geo<D>;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + G::BAR_OFF);
+  uint64_t *q_full = bars + 0;
+  uint64_t *k_full = bars + 1;   // [2]
+  uint64_t *k_empty = bars + 3;  // [2]
+  uint64_t *v_full = bars + 5;   // [2]
+  uint64_t *v_empty = bars + 7;  // [2]
+  uint64_t *s_full = bars + 9;   // [2]
+  uint64_t *p_ready = bars + 11;
+  uint64_t *pv_done = bars + 12;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 13);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int bh = blockIdx.x;
+  const int b = bh / a.H;
+  const int h = bh % a.H;
+  const int qt = a.n_qtiles - 1 - static_cast<int>(blockIdx.y);  // heaviest causal tiles first
+  const int q0 = qt * BM;
+  const int kv_tiles_all = (a.Sk + BN - 1) / BN;
+  int n_kv = kv_tiles_all;
+  if (a.causal) {
+    const int last_q = min(q0 + BM, a.Sq) - 1;
+    const int lim = last_q / BN + 1;
+    n_kv = min(n_kv, lim);
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(q_full), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&k_full[s]), 1);
+      mbar_init(smem_u32(&k_empty[s]), 1);
+      mbar_init(smem_u32(&v_full[s]), 1);
+      mbar_init(smem_u32(&v_empty[s]), 1);
+      mbar_init(smem_u32(&s_full[s]), 1);
+    }
+    mbar_init(smem_u32(p_ready), kSoftmaxThreads);
+    mbar_init(smem_u32(pv_done), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const uint32_t sQ = smem_u32(smem + G::Q_OFF);
+  const uint32_t sK = smem_u32(smem + G::K_OFF);
+  const uint32_t sV = smem_u32(smem + G::V_OFF);
+  const uint32_t sP = smem_u32(smem + G::P_OFF);
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0 && n_kv > 0) {
+      const uint32_t qb = smem_u32(q_full);
+      mbar_arrive_expect_tx(qb, G::TILE_BYTES);
+#pragma unroll
+      for (int c = 0; c < G::CHUNKS; ++c)
+        tma_load_4d(sQ + c * G::CHUNK_BYTES, &tm_q, qb, c * (G::SWB / 2), q0, h, b);
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j & 1;
+        const uint32_t par = ((j >> 1) & 1) ^ 1;
+        if (!mbar_wait(smem_u32(&k_empty[s]), par, abort_flag, &g_flash_status,
+                       TLLM_DEV_WAIT_TIMEOUT + SITE_KEMPTY))
+          break;
+        const uint32_t kb = smem_u32(&k_full[s]);
+        mbar_arrive_expect_tx(kb, G::TILE_BYTES);
+#pragma unroll
+        for (int c = 0; c < G::CHUNKS; ++c)
+          tma_load_4d(sK + s * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_k, kb, c * (G::SWB / 2),
+                      j * BN, h, b);
+        if (!mbar_wait(smem_u32(&v_empty[s]), par, abort_flag, &g_flash_status,
+                       TLLM_DEV_WAIT_TIMEOUT + SITE_VEMPTY))
+          break;
+        const uint32_t vb = smem_u32(&v_full[s]);
+        mbar_arrive_expect_tx(vb, G::TILE_BYTES);
+#pragma unroll
+        for (int c = 0; c < G::CHUNKS; ++c)
+          tma_load_4d(sV + s * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_v, vb, c * (G::SWB / 2),
+                      j * BN, h, b);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ UMMA issuer -------------------------------
+    if (lane == 0 && n_kv > 0) {
+      const uint32_t idesc_qk = make_idesc_f16(BM, BN, kBF16, false, false);
+      const uint32_t idesc_pv = make_idesc_f16(BM, D, kBF16, false, true);
+      bool ok = mbar_wait(smem_u32(q_full), 0, abort_flag, &g_flash_status,
+                          TLLM_DEV_WAIT_TIMEOUT + SITE_Q);
+      auto issue_qk = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(smem_u32(&k_full[s]), (j >> 1) & 1, abort_flag, &g_flash_status,
+                       TLLM_DEV_WAIT_TIMEOUT + SITE_KFULL))
+          return false;
+        tc_fence_after();
+        const uint32_t kbase = sK + s * G::TILE_BYTES;
+        const uint32_t d_tmem = tmem_base + S_COL0 + s * BN;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k)
+          umma_f16_ss(d_tmem, kmajor_desc<D>(sQ, k), kmajor_desc<D>(kbase, k), idesc_qk,
+                      k != 0 ? 1u : 0u);
+        umma_commit(smem_u32(&k_empty[s]));
+        umma_commit(smem_u32(&s_full[s]));
+        return true;
+      };
+      if (ok) ok = issue_qk(0);
+      if (ok && n_kv > 1) ok = issue_qk(1);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(smem_u32(p_ready), j & 1, abort_flag, &g_flash_status,
+                       TLLM_DEV_WAIT_TIMEOUT + SITE_PREADY))
+          break;
+        if (!mbar_wait(smem_u32(&v_full[s]), (j >> 1) & 1, abort_flag, &g_flash_status,
+                       TLLM_DEV_WAIT_TIMEOUT + SITE_VFULL))
+          break;
+        tc_fence_after();
+        const uint32_t vbase = sV + s * G::TILE_BYTES;
+#pragma unroll
+        for (int k = 0; k < BN / 16; ++k) {
+          // P: K-major (key index), two 64-key chunks of 16 KB, 128B swizzle.
+          const uint64_t adesc =
+              make_sdesc(sP + (k >> 2) * (BM * 128) + (k & 3) * 32, 16, 1024, kSwizzle128B);
+          // V: N-major (head dim), swizzle-span chunks CHUNK_BYTES apart (LBO), 8-key groups
+          // 8*SWB apart (SBO); 16 keys = 16 rows of SWB bytes.
+          const uint64_t bdesc =
+              make_sdesc(vbase + k * 16 * G::SWB, G::CHUNK_BYTES, 8 * G::SWB, G::LAYOUT);
+          umma_f16_ss(tmem_base + O_COL, adesc, bdesc, idesc_pv, (j | k) != 0 ? 1u : 0u);
+        }
+        umma_commit(smem_u32(&v_empty[s]));
+        umma_commit(smem_u32(pv_done));
+        if (j + 2 < n_kv) ok = issue_qk(j + 2);
+      }
+    }
+  } else {
+    // ------------------------------ softmax / epilogue ------------------------
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const int qg = q0 + row;  // global query index of this thread's row
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    bool ok = true;
+    uint8_t *prow = smem + G::P_OFF + row * 128;
+    for (int j = 0; j < n_kv; ++j) {
+      const int s = j & 1;
+      if (!mbar_wait(smem_u32(&s_full[s]), (j >> 1) & 1, abort_flag, &g_flash_status,
+                     TLLM_DEV_WAIT_TIMEOUT + SITE_SFULL)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sv[BN];
+#pragma unroll
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + lane_off + S_COL0 + s * BN + c, r);
+#pragma unroll
+        for (int t = 0; t < 32; ++t) sv[c + t] = __uint_as_float(r[t]) * a.scale_log2;
+      }
+      const int k0 = j * BN;
+      const bool need_mask = (k0 + BN > a.Sk) || (a.causal && k0 + BN - 1 > q0);
+      if (need_mask) {
+#pragma unroll
+        for (int t = 0; t < BN; ++t) {
+          const int kg = k0 + t;
+          if (kg >= a.Sk || (a.causal && kg > qg)) sv[t] = -INFINITY;
+        }
+      }
+      float mx = m_run;
+#pragma unroll
+      for (int t = 0; t < BN; ++t) mx = fmaxf(mx, sv[t]);
+      const float m_use = mx == -INFINITY ? 0.f : mx;
+      const float alpha = exp2f(m_run - m_use);
+      float psum = 0.f;
+      // Wait for P_{j-1} V_{j-1} before overwriting P and touching O.
+      if (j > 0) {
+        if (!mbar_wait(smem_u32(pv_done), (j - 1) & 1, abort_flag, &g_flash_status,
+                       TLLM_DEV_WAIT_TIMEOUT + SITE_PVDONE)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+#pragma unroll
+      for (int c = 0; c < BN / 8; ++c) {
+        float p[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          p[t] = exp2f(sv[c * 8 + t] - m_use);
+          psum += p[t];
+        }
+        uint4 pk;
+        pk.x = Pack2<T>::pack(p[0], p[1]);
+        pk.y = Pack2<T>::pack(p[2], p[3]);
+        pk.z = Pack2<T>::pack(p[4], p[5]);
+        pk.w = Pack2<T>::pack(p[6], p[7]);
+        const int half = c >> 3;  // 64-key chunk
+        const int piece = c & 7;  // 16-byte piece within the 128-byte row
+        *reinterpret_cast<uint4 *>(prow + half * (BM * 128) + ((piece ^ (row & 7)) << 4)) = pk;
+      }
+      l_run = l_run * alpha + psum;
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll 1
+        for (int c = 0; c < D; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tmem_base + lane_off + O_COL + c, r);
+#pragma unroll
+          for (int t = 0; t < 32; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * alpha);
+          tmem_st32(tmem_base + lane_off + O_COL + c, r);
+        }
+      }
+      m_run = mx;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(smem_u32(p_ready));
+    }
+    // ---- epilogue: O / l -> global ----
+    if (ok && n_kv > 0 &&
+        mbar_wait(smem_u32(pv_done), (n_kv - 1) & 1, abort_flag, &g_flash_status,
+                  TLLM_DEV_WAIT_TIMEOUT + SITE_PVDONE)) {
+      tc_fence_after();
+      const float inv_l = 1.0f / l_run;
+      T *orow = static_cast<T *>(a.o) + b * a.so0 + h * a.so1 + static_cast<int64_t>(qg) * a.so2;
+#pragma unroll 1
+      for (int c = 0; c < D; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + lane_off + O_COL + c, r);
+        if (qg < a.Sq) {
+          if (a.vec_store) {
+#pragma unroll
+            for (int t = 0; t < 32; t += 8) {
+              uint4 pk;
+              pk.x = Pack2<T>::pack(__uint_as_float(r[t + 0]) * inv_l, __uint_as_float(r[t + 1]) * inv_l);
+              pk.y = Pack2<T>::pack(__uint_as_float(r[t + 2]) * inv_l, __uint_as_float(r[t + 3]) * inv_l);
+              pk.z = Pack2<T>::pack(__uint_as_float(r[t + 4]) * inv_l, __uint_as_float(r[t + 5]) * inv_l);
+              pk.w = Pack2<T>::pack(__uint_as_float(r[t + 6]) * inv_l, __uint_as_float(r[t + 7]) * inv_l);
+              *reinterpret_cast<uint4 *>(orow + c + t) = pk;
+            }
+          } else {
+#pragma unroll
+            for (int t = 0; t < 32; ++t) orow[(c + t) * a.so3] = from_f32<T>(__uint_as_float(r[t]) * inv_l);
+          }
+        }
+      }
+    } else if (n_kv == 0 && qg < a.Sq) {
+      // No keys: softmax over an empty set is 0/0, as in the reference.
+      T *orow = static_cast<T *>(a.o) + b * a.so0 + h * a.so1 + static_cast<int64_t>(qg) * a.so2;
+      for (int c = 0; c < D; ++c) orow[c * a.so3] = from_f32<T>(NAN);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <typename T, int D>
+int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, int64_t H,
+             int64_t Sq, int64_t Sk, const int64_t *sq, const int64_t *sk, const int64_t *sv,
+             const int64_t *so, float sm_scale, int causal, cudaStream_t st) {
+  using G = Geo<D>;
+  const CUtensorMapDataType dt = std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                                 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUtensorMapSwizzle sw = G::SWB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : (G::SWB == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+  const uint32_t box[4] = {static_cast<uint32_t>(G::SWB / 2), static_cast<uint32_t>(BM), 1, 1};
+  CUtensorMap mq, mk, mv;
+  {
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)Sq, (uint64_t)H, (uint64_t)B};
+    const uint64_t str[3] = {(uint64_t)sq[2] * 2, (uint64_t)sq[1] * 2, (uint64_t)sq[0] * 2};
+    int rc = encode_tiled(&mq, dt, 4, const_cast<void *>(q), dims, str, box, sw);
+    if (rc) return rc;
+  }
+  {
+    // Sk == 0 launches no key loads; the map still needs a non-zero extent.
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)(Sk > 0 ? Sk : 1), (uint64_t)H, (uint64_t)B};
+    const uint64_t strk[3] = {(uint64_t)sk[2] * 2, (uint64_t)sk[1] * 2, (uint64_t)sk[0] * 2};
+    int rc = encode_tiled(&mk, dt, 4, const_cast<void *>(k), dims, strk, box, sw);
+    if (rc) return rc;
+    const uint64_t strv[3] = {(uint64_t)sv[2] * 2, (uint64_t)sv[1] * 2, (uint64_t)sv[0] * 2};
+    rc = encode_tiled(&mv, dt, 4, const_cast<void *>(v), dims, strv, box, sw);
+    if (rc) return rc;
+  }
+  Args a;
+  a.o = o;
+  a.so0 = so[0];
+  a.so1 = so[1];
+  a.so2 = so[2];
+  a.so3 = so[3];
+  a.H = static_cast<int>(H);
+  a.Sq = static_cast<int>(Sq);
+  a.Sk = static_cast<int>(Sk);
+  a.n_qtiles = static_cast<int>((Sq + BM - 1) / BM);
+  a.scale_log2 = sm_scale * kLog2e;
+  a.causal = causal ? 1 : 0;
+  a.vec_store = (so[3] == 1 && so[0] % 8 == 0 && so[1] % 8 == 0 && so[2] % 8 == 0 && aligned16(o)) ? 1 : 0;
+  auto kern = flash_fwd_kernel<T, D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(flash)");
+  dim3 grid(static_cast<unsigned>(B * H), static_cast<unsigned>(a.n_qtiles));
+  kern<<<grid, kThreads, G::SMEM_BYTES, st>>>(mq, mk, mv, a);
+  return cuda_status(cudaGetLastError(), "flash launch");
+}
+
+template <typename T>
+int launch(const void *q, const void *k, const void *v, void *o, int64_t B, int64_t H, int64_t Sq,
+           int64_t Sk, int64_t D, const int64_t *sq, const int64_t *sk, const int64_t *sv,
+           const int64_t *so, float sm_scale, int causal, cudaStream_t st) {
+  switch (D) {
+    case 16: return launch_d<T, 16>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, st);
+    case 32: return launch_d<T, 32>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, st);
+    case 64: return launch_d<T, 64>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, st);
+    default: return launch_d<T, 128>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, st);
+  }
+}
+
+}  // namespace
+}  // namespace flash
+}  // namespace tllm
+
+extern "C" int tllm_flash_attn_fwd(const void *q, const void *k, const void *v, void *o,
+                                   int64_t B, int64_t H, int64_t Sq, int64_t Sk, int64_t D,
+                                   const int64_t *sq, const int64_t *sk, const int64_t *sv,
+                                   const int64_t *so, float sm_scale, int causal, int dtype,
+                                   void *stream) {
+  using namespace tllm;
+  clear_error();
+  TLLM_CHECK_ARG(B >= 0 && H >= 0 && Sq >= 0 && Sk >= 0, "flash_attention: negative dimension");
+  TLLM_CHECK_ARG(D == 16 || D == 32 || D == 64 || D == 128,
+                 "flash_attention: head dim %lld not in {16,32,64,128}", (long long)D);
+  TLLM_CHECK_ARG(dtype == TLLM_DTYPE_F16 || dtype == TLLM_DTYPE_BF16,
+                 "flash_attention: unsupported dtype %d", dtype);
+  TLLM_CHECK_ARG(sq && sk && sv && so, "flash_attention: null stride array");
+  if (B == 0 || H == 0 || Sq == 0) return TLLM_OK;
+  TLLM_CHECK_ARG(q && k && v && o, "flash_attention: null tensor pointer");
+  TLLM_CHECK_ARG(Sq < (1LL << 31) && Sk < (1LL << 31) && B * H < (1LL << 31),
+                 "flash_attention: problem too large");
+  TLLM_CHECK_ARG((Sq + 127) / 128 <= 65535, "flash_attention: Sq above 8388480 is not supported");
+  TLLM_CHECK_ARG(sq[3] == 1 && sk[3] == 1 && sv[3] == 1,
+                 "flash_attention: q/k/v need a unit innermost stride");
+  for (int i = 0; i < 3; ++i)
+    TLLM_CHECK_ARG(sq[i] % 8 == 0 && sk[i] % 8 == 0 && sv[i] % 8 == 0,
+                   "flash_attention: q/k/v strides must be multiples of 8 elements");
+  TLLM_CHECK_ARG(flash::aligned16(q) && flash::aligned16(k) && flash::aligned16(v),
+                 "flash_attention: q/k/v must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == TLLM_DTYPE_F16)
+    return flash::launch<__half>(q, k, v, o, B, H, Sq, Sk, D, sq, sk, sv, so, sm_scale, causal, st);
+  return flash::launch<__nv_bfloat16>(q, k, v, o, B, H, Sq, Sk, D, sq, sk, sv, so, sm_scale, causal,
+                                      st);
+}

@@ -1,0 +1,205 @@
+// Fused RMSNorm + rotate-half RoPE for sm_100a.
+//
+// Reference: python/triton_llm/ops/rmsnorm_rope.py:9-75 (one Triton program per (b,s,h)
+// row, 4 warps each) and the oracle python/triton_llm/reference/norm_rope.py:12-40.
+//
+// B200 design: the op is pure HBM streaming (2 bytes in + 2 bytes out per element plus the
+// small cos/sin/weight tables that stay in L2), so a row of D elements is handled by D/16
+// threads, each owning one 16-byte vector of the first half and the matching vector of the
+// second half; the sum of squares is reduced with warp shuffles inside that thread group and
+// the rotate-half pairing (i, i + D/2) never leaves the thread's registers.
+//
+// Numerics follow the oracle: variance and scaling in fp32, the normalised value
+// x * rstd * w rounded to the I/O dtype (norm_rope.py:15), then RoPE in fp32 with one
+// rounding per product (norm_rope.py:28-29), stored in the I/O dtype.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "common.h"
+#include "ptx.cuh"
+
+namespace tllm {
+namespace {
+
+struct RowGeom {
+  int64_t S, H;
+  int64_t sxb, sxs, sxh, sxd;
+  int64_t sob, sos, soh, sod;
+  int64_t scs, scd, sss, ssd, sw;
+};
+
+template <typename T>
+__device__ __forceinline__ void load8(const T *p, float (&v)[8]) {
+  const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(p));
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = Pack2<T>::unpack(w[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void store8(T *p, const float (&v)[8]) {
+  uint4 raw;
+  raw.x = Pack2<T>::pack(v[0], v[1]);
+  raw.y = Pack2<T>::pack(v[2], v[3]);
+  raw.z = Pack2<T>::pack(v[4], v[5]);
+  raw.w = Pack2<T>::pack(v[6], v[7]);
+  *reinterpret_cast<uint4 *>(p) = raw;
+}
+
+template <typename T>
+__device__ __forceinline__ float round_io(float v) {
+  return to_f32<T>(from_f32<T>(v));
+}
+
+// Vector path: unit inner strides, 16-byte aligned rows. TPR = D / 16 threads per row.
+template <typename T, int D>
+__global__ void __launch_bounds__(256) rmsnorm_rope_vec_kernel(
+    const T *__restrict__ x, const T *__restrict__ w, const T *__restrict__ cosb,
+    const T *__restrict__ sinb, T *__restrict__ out, int64_t rows, RowGeom g, float eps) {
+  constexpr int TPR = D / 16;
+  constexpr int HALF = D / 2;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t row = tid / TPR;
+  const int part = static_cast<int>(tid % TPR);
+  // All TPR lanes of a row are in the same warp (TPR divides 32), so shuffles are safe even
+  // for the ragged last row group; lanes past the end compute on a clamped row and skip the
+  // store.
+  const bool valid = row < rows;
+  const int64_t r = valid ? row : rows - 1;
+  const int64_t h = r % g.H;
+  const int64_t bs = r / g.H;
+  const int64_t s = bs % g.S;
+  const int64_t b = bs / g.S;
+
+  const T *xr = x + b * g.sxb + s * g.sxs + h * g.sxh;
+  const int c = part * 8;
+  float x1[8], x2[8], w1[8], w2[8];
+  load8<T>(xr + c, x1);
+  load8<T>(xr + HALF + c, x2);
+  load8<T>(w + c, w1);
+  load8<T>(w + HALF + c, w2);
+
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss = fmaf(x1[i], x1[i], fmaf(x2[i], x2[i], ss));
+#pragma unroll
+  for (int off = TPR / 2; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float rstd = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), eps));
+
+  float c1[8], c2[8], s1[8], s2[8];
+  load8<T>(cosb + s * g.scs + c, c1);
+  load8<T>(cosb + s * g.scs + HALF + c, c2);
+  load8<T>(sinb + s * g.sss + c, s1);
+  load8<T>(sinb + s * g.sss + HALF + c, s2);
+
+  float o1[8], o2[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float y1 = round_io<T>(__fmul_rn(__fmul_rn(x1[i], rstd), w1[i]));
+    const float y2 = round_io<T>(__fmul_rn(__fmul_rn(x2[i], rstd), w2[i]));
+    o1[i] = __fsub_rn(__fmul_rn(y1, c1[i]), __fmul_rn(y2, s1[i]));
+    o2[i] = __fadd_rn(__fmul_rn(y2, c2[i]), __fmul_rn(y1, s2[i]));
+  }
+  if (valid) {
+    T *orow = out + b * g.sob + s * g.sos + h * g.soh;
+    store8<T>(orow + c, o1);
+    store8<T>(orow + HALF + c, o2);
+  }
+}
+
+// General-stride path: one thread per row (any strides, any alignment).
+template <typename T>
+__global__ void __launch_bounds__(128) rmsnorm_rope_strided_kernel(
+    const T *__restrict__ x, const T *__restrict__ w, const T *__restrict__ cosb,
+    const T *__restrict__ sinb, T *__restrict__ out, int64_t rows, int D, RowGeom g,
+    float eps) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const int64_t h = row % g.H;
+  const int64_t bs = row / g.H;
+  const int64_t s = bs % g.S;
+  const int64_t b = bs / g.S;
+  const T *xr = x + b * g.sxb + s * g.sxs + h * g.sxh;
+  T *orow = out + b * g.sob + s * g.sos + h * g.soh;
+  const int half = D / 2;
+  float ss = 0.f;
+  for (int i = 0; i < D; ++i) {
+    const float v = to_f32<T>(xr[i * g.sxd]);
+    ss = fmaf(v, v, ss);
+  }
+  const float rstd = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), eps));
+  for (int i = 0; i < half; ++i) {
+    const float y1 =
+        round_io<T>(__fmul_rn(__fmul_rn(to_f32<T>(xr[i * g.sxd]), rstd), to_f32<T>(w[i * g.sw])));
+    const float y2 = round_io<T>(__fmul_rn(__fmul_rn(to_f32<T>(xr[(i + half) * g.sxd]), rstd),
+                                           to_f32<T>(w[(i + half) * g.sw])));
+    const float ca = to_f32<T>(cosb[s * g.scs + i * g.scd]);
+    const float cb = to_f32<T>(cosb[s * g.scs + (i + half) * g.scd]);
+    const float sa = to_f32<T>(sinb[s * g.sss + i * g.ssd]);
+    const float sb = to_f32<T>(sinb[s * g.sss + (i + half) * g.ssd]);
+    orow[i * g.sod] = from_f32<T>(__fsub_rn(__fmul_rn(y1, ca), __fmul_rn(y2, sa)));
+    orow[(i + half) * g.sod] = from_f32<T>(__fadd_rn(__fmul_rn(y2, cb), __fmul_rn(y1, sb)));
+  }
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <typename T>
+int launch(const void *x, const void *w, const void *c, const void *s, void *o, int64_t rows,
+           int64_t D, const RowGeom &g, bool vec, float eps, cudaStream_t st) {
+  const T *xp = static_cast<const T *>(x);
+  const T *wp = static_cast<const T *>(w);
+  const T *cp = static_cast<const T *>(c);
+  const T *sp = static_cast<const T *>(s);
+  T *op = static_cast<T *>(o);
+  if (vec) {
+    const int64_t threads = rows * (D / 16);
+    const unsigned grid = static_cast<unsigned>((threads + 255) / 256);
+    switch (D) {
+      case 16: rmsnorm_rope_vec_kernel<T, 16><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
+      case 32: rmsnorm_rope_vec_kernel<T, 32><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
+      case 64: rmsnorm_rope_vec_kernel<T, 64><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
+      default: rmsnorm_rope_vec_kernel<T, 128><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
+    }
+  } else {
+    const unsigned grid = static_cast<unsigned>((rows + 127) / 128);
+    rmsnorm_rope_strided_kernel<T><<<grid, 128, 0, st>>>(xp, wp, cp, sp, op, rows,
+                                                         static_cast<int>(D), g, eps);
+  }
+  return cuda_status(cudaGetLastError(), "rmsnorm_rope launch");
+}
+
+}  // namespace
+}  // namespace tllm
+
+extern "C" int tllm_rmsnorm_rope(const void *x, const void *w, const void *cos, const void *sin,
+                                 void *out, int64_t B, int64_t S, int64_t H, int64_t D,
+                                 const int64_t *sx, int64_t sw, const int64_t *scos,
+                                 const int64_t *ssin, const int64_t *so, float eps, int dtype,
+                                 void *stream) {
+  using namespace tllm;
+  clear_error();
+  TLLM_CHECK_ARG(B >= 0 && S >= 0 && H >= 0, "rmsnorm_rope: negative dimension");
+  TLLM_CHECK_ARG(D == 16 || D == 32 || D == 64 || D == 128,
+                 "rmsnorm_rope: head dim %lld not in {16,32,64,128}", (long long)D);
+  TLLM_CHECK_ARG(dtype == TLLM_DTYPE_F16 || dtype == TLLM_DTYPE_BF16,
+                 "rmsnorm_rope: unsupported dtype %d", dtype);
+  TLLM_CHECK_ARG(sx && scos && ssin && so, "rmsnorm_rope: null stride array");
+  const int64_t rows = B * S * H;
+  if (rows == 0) return TLLM_OK;
+  TLLM_CHECK_ARG(x && w && cos && sin && out, "rmsnorm_rope: null tensor pointer");
+  RowGeom g{S,       H,       sx[0],   sx[1],   sx[2],   sx[3], so[0], so[1],
+            so[2],   so[3],   scos[0], scos[1], ssin[0], ssin[1], sw};
+  const bool vec = sx[3] == 1 && so[3] == 1 && scos[1] == 1 && ssin[1] == 1 && sw == 1 &&
+                   sx[0] % 8 == 0 && sx[1] % 8 == 0 && sx[2] % 8 == 0 && so[0] % 8 == 0 &&
+                   so[1] % 8 == 0 && so[2] % 8 == 0 && scos[0] % 8 == 0 && ssin[0] % 8 == 0 &&
+                   aligned16(x) && aligned16(out) && aligned16(w) && aligned16(cos) &&
+                   aligned16(sin);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == TLLM_DTYPE_F16) return launch<__half>(x, w, cos, sin, out, rows, D, g, vec, eps, st);
+  return launch<__nv_bfloat16>(x, w, cos, sin, out, rows, D, g, vec, eps, st);
+}

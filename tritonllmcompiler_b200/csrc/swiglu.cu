@@ -1,0 +1,381 @@
+// SwiGLU dual GEMM for sm_100a: out = silu(x @ w1) * (x @ w3).
+//
+// Reference: python/triton_llm/ops/swiglu.py:11-76 (Triton, two register accumulators fed
+// by shared x tile loads, silu(g)*u epilogue at :47-51) and the oracle
+// python/triton_llm/reference/swiglu.py:12-15.
+//
+// B200 design (persistent, warp-specialised, one CTA per SM):
+//   warp 0      TMA producer: per K-step one x tile [128 x 64] (K-major, 128B swizzle) and
+//               the matching w1 and w3 tiles [64 x 128] (N-major) into a 4-stage ring.
+//   warp 1      allocates 512 TMEM columns, then one lane issues tcgen05.mma: the w1 and w3
+//               tiles sit side by side in shared memory as ONE N=256 operand, so a single
+//               128x256x16 UMMA per k16 step computes [x@w1 | x@w3] into adjacent TMEM
+//               columns (the x tile is read once for both products).
+//   warps 2-5   epilogue: tcgen05.ld the two fp32 accumulators of a row, silu(g)*u in fp32,
+//               one store in the I/O dtype. The accumulator is double-buffered in TMEM
+//               (2 x 256 columns) so the epilogue of tile i overlaps the main loop of i+1.
+// No TMA multicast is used anywhere. Every mbarrier wait is bounded.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "common.h"
+#include "ptx.cuh"
+
+namespace tllm {
+
+__device__ int g_swiglu_status = 0;
+
+int swiglu_read_status(int *out) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_swiglu_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_status(e, "cudaMemcpyFromSymbol(swiglu status)");
+  const int zero = 0;
+  e = cudaMemcpyToSymbol(g_swiglu_status, &zero, sizeof(int));
+  if (e != cudaSuccess) return cuda_status(e, "cudaMemcpyToSymbol(swiglu status)");
+  *out = v;
+  return TLLM_OK;
+}
+
+namespace swiglu {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 128;  // output columns per tile (each of w1 and w3)
+constexpr int BK = 64;   // one 128-byte swizzle row of fp16
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;                 // 16 KB
+constexpr int B_CHUNK_BYTES = BK * 64 * 2;           // 8 KB: 64 N-columns x BK rows
+constexpr int B_BYTES = 4 * B_CHUNK_BYTES;           // w1[0:64] w1[64:128] w3[0:64] w3[64:128]
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;       // 48 KB
+constexpr int ACC_COLS = 2 * BN;                     // G | U
+constexpr int TMEM_COLS = 512;                       // two accumulator buffers
+constexpr int kThreads = 192;
+constexpr int kEpiThreads = 128;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*barriers*/ + 1024 /*alignment*/;
+
+enum : int {
+  SITE_EMPTY = 1,
+  SITE_FULL = 2,
+  SITE_TEMPTY = 3,
+  SITE_TFULL = 4,
+};
+
+struct Geom {
+  int M, N, K;
+  int tiles_m, tiles_n, k_blocks;
+  int64_t ldo;
+  int vec_store;  // 16-byte stores allowed (ldo % 8 == 0 and out 16-byte aligned)
+};
+
+template <typename T>
+__device__ __forceinline__ void store_row_chunk(T *orow, int n_base, int N, bool vec,
+                                                const float (&v)[32]) {
+  if (vec && n_base + 32 <= N) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      uint4 raw;
+      raw.x = Pack2<T>::pack(v[j + 0], v[j + 1]);
+      raw.y = Pack2<T>::pack(v[j + 2], v[j + 3]);
+      raw.z = Pack2<T>::pack(v[j + 4], v[j + 5]);
+      raw.w = Pack2<T>::pack(v[j + 6], v[j + 7]);
+      *reinterpret_cast<uint4 *>(orow + n_base + j) = raw;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (n_base + j < N) orow[n_base + j] = from_f32<T>(v[j]);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
+                     const __grid_constant__ CUtensorMap tm_w1,
+                     const __grid_constant__ CUtensorMap tm_w3, T *__restrict__ out,
+                     const Geom g) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+  uint64_t *full = bars;
+  uint64_t *empty = bars + STAGES;
+  uint64_t *tfull = bars + 2 * STAGES;
+  uint64_t *tempty = bars + 2 * STAGES + 2;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  constexpr bool kBF16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), kEpiThreads);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_w1);
+    tma_prefetch_desc(&tm_w3);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const int num_tiles = g.tiles_m * g.tiles_n;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile % g.tiles_m) * BM;
+        const int n0 = (tile / g.tiles_m) * BN;
+        for (int kb = 0; kb < g.k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1, abort_flag, &g_swiglu_status,
+                         TLLM_DEV_WAIT_TIMEOUT + SITE_EMPTY)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&full[stage]);
+          mbar_arrive_expect_tx(fb, STAGE_BYTES);
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+          const int k0 = kb * BK;
+          tma_load_2d(sa, &tm_x, fb, k0, m0);
+          tma_load_2d(sb + 0 * B_CHUNK_BYTES, &tm_w1, fb, n0, k0);
+          tma_load_2d(sb + 1 * B_CHUNK_BYTES, &tm_w1, fb, n0 + 64, k0);
+          tma_load_2d(sb + 2 * B_CHUNK_BYTES, &tm_w3, fb, n0, k0);
+          tma_load_2d(sb + 3 * B_CHUNK_BYTES, &tm_w3, fb, n0 + 64, k0);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ UMMA issuer -------------------------------
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_f16(BM, 2 * BN, kBF16, false, true);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1, abort_flag, &g_swiglu_status,
+                       TLLM_DEV_WAIT_TIMEOUT + SITE_TEMPTY)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
+        for (int kb = 0; kb < g.k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, &g_swiglu_status,
+                         TLLM_DEV_WAIT_TIMEOUT + SITE_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // A: K-major, 128B swizzle, 8-row groups 1024 B apart; step 16 elements = 32 B.
+            const uint64_t adesc = make_sdesc(sa + k * 32, 16, 1024, kSwizzle128B);
+            // B: N-major, 128B swizzle; 64-column atoms 8 KB apart (LBO), 8-row K groups
+            // 1024 B apart (SBO); step 16 K rows = 2048 B.
+            const uint64_t bdesc = make_sdesc(sb + k * 2048, B_CHUNK_BYTES, 1024, kSwizzle128B);
+            umma_f16_ss(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(smem_u32(&empty[stage]));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(&tfull[acc]));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // ------------------------------ epilogue ----------------------------------
+    const int quad = warp & 3;  // TMEM lanes this warp may access
+    const int row = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag, &g_swiglu_status,
+                     TLLM_DEV_WAIT_TIMEOUT + SITE_TFULL))
+        break;
+      tc_fence_after();
+      const int m0 = (tile % g.tiles_m) * BM;
+      const int n0 = (tile / g.tiles_m) * BN;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * ACC_COLS;
+      const int m = m0 + row;
+      T *orow = out + static_cast<int64_t>(m) * g.ldo;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t gr[32], ur[32];
+        tmem_ld32(t_row + c, gr);
+        tmem_ld32(t_row + BN + c, ur);
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float gv = __uint_as_float(gr[j]);
+          const float uv = __uint_as_float(ur[j]);
+          v[j] = (gv / (1.0f + expf(-gv))) * uv;
+        }
+        if (m < g.M) store_row_chunk<T>(orow, n0 + c, g.N, g.vec_store != 0, v);
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&tempty[acc]));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// Layout-agnostic fallback (CUDA cores, fp32 accumulation) for shapes whose strides or
+// alignment a TMA descriptor cannot describe: K or N not a multiple of 8, odd strides.
+template <typename T>
+__global__ void __launch_bounds__(256) swiglu_simt_kernel(const T *__restrict__ x,
+                                                          const T *__restrict__ w1,
+                                                          const T *__restrict__ w3,
+                                                          T *__restrict__ out, int M, int N,
+                                                          int K, int64_t lda, int64_t ldb1,
+                                                          int64_t ldb3, int64_t ldo) {
+  __shared__ float xs[16][17];
+  __shared__ float w1s[16][17];
+  __shared__ float w3s[16][17];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m = blockIdx.y * 16 + ty;
+  const int n = blockIdx.x * 16 + tx;
+  float gacc = 0.f, uacc = 0.f;
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    xs[ty][tx] = (m < M && k0 + tx < K) ? to_f32<T>(x[static_cast<int64_t>(m) * lda + k0 + tx]) : 0.f;
+    const int kr = k0 + ty;
+    w1s[ty][tx] = (kr < K && n < N) ? to_f32<T>(w1[static_cast<int64_t>(kr) * ldb1 + n]) : 0.f;
+    w3s[ty][tx] = (kr < K && n < N) ? to_f32<T>(w3[static_cast<int64_t>(kr) * ldb3 + n]) : 0.f;
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      gacc = fmaf(xs[ty][kk], w1s[kk][tx], gacc);
+      uacc = fmaf(xs[ty][kk], w3s[kk][tx], uacc);
+    }
+    __syncthreads();
+  }
+  if (m < M && n < N)
+    out[static_cast<int64_t>(m) * ldo + n] = from_f32<T>((gacc / (1.0f + expf(-gacc))) * uacc);
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <typename T>
+int launch(const void *x, const void *w1, const void *w3, void *out, int64_t M, int64_t N,
+           int64_t K, int64_t lda, int64_t ldb1, int64_t ldb3, int64_t ldo, cudaStream_t st) {
+  const bool tma_ok = lda % 8 == 0 && ldb1 % 8 == 0 && ldb3 % 8 == 0 && aligned16(x) &&
+                      aligned16(w1) && aligned16(w3) && K % 8 == 0 && N % 8 == 0;
+  if (!tma_ok) {
+    dim3 grid(static_cast<unsigned>((N + 15) / 16), static_cast<unsigned>((M + 15) / 16));
+    swiglu_simt_kernel<T><<<grid, 256, 0, st>>>(
+        static_cast<const T *>(x), static_cast<const T *>(w1), static_cast<const T *>(w3),
+        static_cast<T *>(out), static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+        lda, ldb1, ldb3, ldo);
+    return cuda_status(cudaGetLastError(), "swiglu fallback launch");
+  }
+  const CUtensorMapDataType dt =
+      std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap mx, m1, m3;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(lda) * 2};
+    const uint32_t box[2] = {BK, BM};
+    int rc = encode_tiled(&mx, dt, 2, const_cast<void *>(x), dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(K)};
+    const uint32_t box[2] = {64, BK};
+    const uint64_t s1[1] = {static_cast<uint64_t>(ldb1) * 2};
+    int rc = encode_tiled(&m1, dt, 2, const_cast<void *>(w1), dims, s1, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    const uint64_t s3[1] = {static_cast<uint64_t>(ldb3) * 2};
+    rc = encode_tiled(&m3, dt, 2, const_cast<void *>(w3), dims, s3, box,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  Geom g;
+  g.M = static_cast<int>(M);
+  g.N = static_cast<int>(N);
+  g.K = static_cast<int>(K);
+  g.tiles_m = static_cast<int>((M + BM - 1) / BM);
+  g.tiles_n = static_cast<int>((N + BN - 1) / BN);
+  g.k_blocks = static_cast<int>((K + BK - 1) / BK);
+  g.ldo = ldo;
+  g.vec_store = (ldo % 8 == 0 && aligned16(out)) ? 1 : 0;
+  auto kern = swiglu_tc_kernel<T>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(swiglu)");
+  const int num_tiles = g.tiles_m * g.tiles_n;
+  const int sms = sm_count();
+  const int grid = num_tiles < sms ? num_tiles : sms;
+  kern<<<grid, kThreads, SMEM_BYTES, st>>>(mx, m1, m3, static_cast<T *>(out), g);
+  return cuda_status(cudaGetLastError(), "swiglu launch");
+}
+
+}  // namespace
+}  // namespace swiglu
+}  // namespace tllm
+
+extern "C" int tllm_swiglu(const void *x, const void *w1, const void *w3, void *out, int64_t M,
+                           int64_t N, int64_t K, int64_t lda, int64_t ldb1, int64_t ldb3,
+                           int64_t ldo, int dtype, void *stream) {
+  using namespace tllm;
+  clear_error();
+  TLLM_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "swiglu: negative dimension");
+  TLLM_CHECK_ARG(dtype == TLLM_DTYPE_F16 || dtype == TLLM_DTYPE_BF16, "swiglu: unsupported dtype %d",
+                 dtype);
+  TLLM_CHECK_ARG(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31), "swiglu: dimension too large");
+  if (M == 0 || N == 0) return TLLM_OK;
+  TLLM_CHECK_ARG(x && w1 && w3 && out, "swiglu: null tensor pointer");
+  TLLM_CHECK_ARG(lda >= K && ldb1 >= N && ldb3 >= N && ldo >= N, "swiglu: leading dimension too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (K == 0) {
+    // x @ w = 0, silu(0) * 0 = 0: a zero fill keeps the contract without a GEMM.
+    return cuda_status(cudaMemset2DAsync(out, static_cast<size_t>(ldo) * 2, 0,
+                                         static_cast<size_t>(N) * 2, static_cast<size_t>(M), st),
+                       "swiglu zero fill");
+  }
+  if (dtype == TLLM_DTYPE_F16)
+    return swiglu::launch<__half>(x, w1, w3, out, M, N, K, lda, ldb1, ldb3, ldo, st);
+  return swiglu::launch<__nv_bfloat16>(x, w1, w3, out, M, N, K, lda, ldb1, ldb3, ldo, st);
+}
