@@ -44,6 +44,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-ops", action="store_true", help="skip the per-operator extras")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--op", choices=sorted(OP_CASES), default=None,
+                    help="run only this operator case (steps+warmup launches) and print its timing")
     return ap.parse_args()
 
 
@@ -196,6 +198,81 @@ def cpu_swiglu_baseline(inputs=None, min_seconds=8.0, rows=512):
 
 
 # ------------------------------------------------------------------------------------------
+# Single-operator cases (used to profile one kernel at a time from committed code).
+OP_CASES = {
+    "swiglu": "swiglu M4096 K4096 N14336 fp16",
+    "flash_causal": "flash_attention causal [4,32,4096,128] fp16",
+    "flash_full": "flash_attention non-causal [4,32,1024,128] fp16",
+    "paged": "paged_attention decode B64 H32 D128 bs16 lens U[512,8192] fp16",
+    "paged_small": "paged_attention decode B16 H32 D128 bs16 lens U[512,8192] fp16",
+    "rmsnorm": "rmsnorm_rope [2,128,8,64] fp16",
+    "rmsnorm_bw": "rmsnorm_rope [16,4096,32,128] fp16",
+}
+
+
+def _paged_inputs(torch, batch, seed=3):
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(512, 8193, (batch,), dtype=torch.int32, generator=g)
+    nb = [(int(n) + 15) // 16 for n in lens]
+    pool = sum(nb)
+    perm = torch.randperm(pool, generator=g)
+    bt = torch.zeros(batch, max(nb), dtype=torch.int32)
+    pos = 0
+    for i, n in enumerate(nb):
+        bt[i, :n] = perm[pos:pos + n].to(torch.int32)
+        pos += n
+    gd = torch.Generator(device="cuda").manual_seed(seed)
+    kc = torch.randn((pool, 16, 32, 128), generator=gd, device="cuda").half()
+    vc = torch.randn((pool, 16, 32, 128), generator=gd, device="cuda").half()
+    q = torch.randn((batch, 32, 1, 128), generator=gd, device="cuda").half()
+    nbytes = int(lens.sum()) * 32 * 128 * 2 * 2 + 2 * batch * 32 * 128 * 2 + sum(nb) * 4 + batch * 4
+    return q, kc, vc, bt.cuda(), lens.cuda(), nbytes
+
+
+def run_op(args):
+    """Runs one operator case warmup+steps times; prints {"op", "ms", "value", "unit"}."""
+    import torch
+
+    import tritonllmcompiler_b200 as T
+
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    gd = torch.Generator(device="cuda").manual_seed(1)
+
+    def rn(shape, scale=1.0):
+        return (torch.randn(shape, generator=gd, device="cuda") * scale).half()
+
+    op = args.op
+    if op == "swiglu":
+        M, K, N = SWIGLU_SHAPE
+        x, w1, w3 = rn((M, K)), rn((K, N), K ** -0.5), rn((K, N), K ** -0.5)
+        fn, work, unit = (lambda: T.swiglu(x, w1, w3)), 4.0 * M * K * N, "TFLOP/s"
+    elif op in ("flash_causal", "flash_full"):
+        causal = op == "flash_causal"
+        s = 4096 if causal else 1024
+        q, k, v = rn((4, 32, s, 128)), rn((4, 32, s, 128)), rn((4, 32, s, 128))
+        fn = lambda: T.flash_attention(q, k, v, causal=causal)  # noqa: E731
+        work, unit = 4.0 * 4 * 32 * s * s * 128 * (0.5 if causal else 1.0), "TFLOP/s"
+    elif op in ("paged", "paged_small"):
+        q, kc, vc, bt, cl, work = _paged_inputs(torch, 64 if op == "paged" else 16)
+        fn, unit = (lambda: T.paged_attention(q, kc, vc, bt, cl, block_size=16)), "GB/s"
+    else:
+        b, s, h, d = (2, 128, 8, 64) if op == "rmsnorm" else (16, 4096, 32, 128)
+        x = rn((b, s, h, d))
+        w = (1 + 0.1 * torch.randn(d, device="cuda")).half()
+        pos = torch.arange(s, device="cuda", dtype=torch.float32)
+        inv = 1.0 / (10000 ** (torch.arange(0, d, 2, device="cuda").float() / d))
+        emb = torch.cat([torch.outer(pos, inv)] * 2, dim=-1)
+        cos, sin = emb.cos().half(), emb.sin().half()
+        fn = lambda: T.rmsnorm_rope(x, w, cos, sin)  # noqa: E731
+        work, unit = 2 * (b * s * h * d * 2) + d * 2 + 2 * (s * d * 2), "GB/s"
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    ts = _events_time(torch, fn, args.steps, args.warmup, flush)
+    ms = statistics.median(ts)
+    scale = 1e12 if unit == "TFLOP/s" else 1e9
+    print(json.dumps({"op": op, "case": OP_CASES[op], "ms": ms, "value": work / (ms * 1e-3) / scale,
+                      "unit": unit, "launches": args.steps + args.warmup}), flush=True)
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -265,26 +342,13 @@ def extra_ops(torch, T, peaks):
                      "roofline_frac": tf / tc, "bound": "tensor"}
         del q, k, v
     # paged_attention decode: B64 H32 D128 bs16, lens U[512,8192] (seed 3).
-    g = torch.Generator().manual_seed(3)
-    lens = torch.randint(512, 8193, (64,), dtype=torch.int32, generator=g)
-    nb = [(int(n) + 15) // 16 for n in lens]
-    pool = sum(nb)
-    perm = torch.randperm(pool, generator=g)
-    bt = torch.zeros(64, max(nb), dtype=torch.int32)
-    pos = 0
-    for i, n in enumerate(nb):
-        bt[i, :n] = perm[pos:pos + n].to(torch.int32)
-        pos += n
-    kc, vc = gen((pool, 16, 32, 128), 5), gen((pool, 16, 32, 128), 6)
-    qd = gen((64, 32, 1, 128), 7)
-    btd, cl = bt.cuda(), lens.cuda()
-    nbytes = int(lens.sum()) * 32 * 128 * 2 * 2 + 2 * 64 * 32 * 128 * 2 + sum(nb) * 4 + 64 * 4
+    qd, kc, vc, btd, cl, nbytes = _paged_inputs(torch, 64)
     ts = _events_time(torch, lambda: T.paged_attention(qd, kc, vc, btd, cl, block_size=16), 20, 5, flush)
     t = statistics.median(ts)
     gbs = nbytes / (t * 1e-3) / 1e9
     res["paged_decode_b64_h32_d128_bs16"] = {"value": gbs, "unit": "GB/s", "ms": t, "bytes": nbytes,
                                               "roofline_frac": gbs / hbm, "bound": "hbm",
-                                              "kv_tokens": int(lens.sum())}
+                                              "kv_tokens": int(cl.sum().item())}
     del kc, vc
     torch.cuda.empty_cache()
     return res
@@ -419,7 +483,9 @@ def run_ours(args):
 
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.op is not None:
+        run_op(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

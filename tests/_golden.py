@@ -9,8 +9,35 @@ import torch
 
 GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
-# The reference's own op-test tolerance (tests/python/test_*.py: ATOL, RTOL = 1e-3, 1e-2).
+# The reference's own op-test tolerance (tests/python/test_*.py: ATOL, RTOL = 1e-3, 1e-2),
+# stated for fp16. bf16 keeps 8 significant bits instead of fp16's 11, so one rounding of
+# a value near 1 (P before P@V, the output itself) is 2^-8 instead of 2^-11: for bf16 the
+# absolute tolerance is scaled by that factor of 8 (rounded up to 1e-2).
 ATOL, RTOL = 1e-3, 1e-2
+BF16_ATOL, BF16_RTOL = 1e-2, 1e-2
+
+
+def tol(dtype) -> dict:
+    """allclose tolerance for an I/O dtype ("fp16"/"bf16" or a torch dtype)."""
+    if dtype in ("bf16", torch.bfloat16):
+        return dict(atol=BF16_ATOL, rtol=BF16_RTOL)
+    return dict(atol=ATOL, rtol=RTOL)
+
+
+def assert_doubled_exactly(a: torch.Tensor, b: torch.Tensor):
+    """b == 2*a exactly wherever 2*a is a normal number of a's dtype.
+
+    Doubling commutes with round-to-nearest except in the subnormal range (below 2^-14 in
+    fp16), where the rounding grid does not scale; there b may differ by one subnormal step.
+    """
+    a2 = a.float() * 2
+    bf = b.float()
+    tiny = torch.finfo(a.dtype).tiny
+    normal = a2.abs() >= tiny
+    bad = (a2 != bf) & normal
+    assert int(bad.sum()) == 0, f"{int(bad.sum())} normal values not doubled exactly"
+    sub_step = tiny * torch.finfo(a.dtype).eps
+    assert float((a2 - bf)[~normal].abs().max().item() if (~normal).any() else 0.0) <= sub_step
 
 TENSOR_KEYS = {"q", "k", "v", "out", "k_cache", "v_cache", "x", "w", "cos", "sin", "w1", "w3"}
 

@@ -10,10 +10,11 @@ pytestmark = pytest.mark.gpu
 
 
 def _close(out: torch.Tensor, ref: torch.Tensor):
+    t = G.tol(ref.dtype)
     out = out.float().cpu()
     ref = ref.float()
     err = (out - ref).abs().max().item() if out.numel() else 0.0
-    assert torch.allclose(out, ref, atol=G.ATOL, rtol=G.RTOL, equal_nan=True), f"max abs err {err}"
+    assert torch.allclose(out, ref, equal_nan=True, **t), f"max abs err {err}"
 
 
 @pytest.mark.parametrize("name", G.names("flash"))

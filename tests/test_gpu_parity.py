@@ -31,7 +31,7 @@ def _assert_close(out, ref_np):
     got = out.float().cpu().numpy()
     assert got.shape == ref_np.shape
     err = np.nanmax(np.abs(got - ref_np)) if got.size else 0.0
-    assert np.allclose(got, ref_np, atol=G.ATOL, rtol=G.RTOL, equal_nan=True), f"max abs err {err}"
+    assert np.allclose(got, ref_np, equal_nan=True, **G.tol(out.dtype)), f"max abs err {err}"
 
 
 # ----------------------------------------------------------------------------- rmsnorm_rope
@@ -79,7 +79,7 @@ def test_rmsnorm_rope_weight_scaling_is_exact(cuda_device):
     cos, sin = _rope(256, 128, torch.float16)
     a = T.rmsnorm_rope(x, w, cos.cuda(), sin.cuda())
     b = T.rmsnorm_rope(x, w * 2, cos.cuda(), sin.cuda())
-    assert torch.equal(a.float() * 2, b.float())
+    G.assert_doubled_exactly(a, b)
 
 
 # ----------------------------------------------------------------------------- swiglu
@@ -123,7 +123,7 @@ def test_swiglu_linearity_in_w3_is_exact(cuda_device):
     w3 = (torch.randn(1024, 768, generator=g) / 32).half().cuda()
     a = T.swiglu(x, w1, w3)
     b = T.swiglu(x, w1, w3 * 2)
-    assert torch.equal(a.float() * 2, b.float())
+    G.assert_doubled_exactly(a, b)
 
 
 # ----------------------------------------------------------------------------- flash
@@ -165,7 +165,7 @@ def test_flash_value_scaling_is_exact(cuda_device):
     v = torch.randn(2, 4, 1024, 128, generator=g).half().cuda()
     a = T.flash_attention(q, k, v, causal=True)
     b = T.flash_attention(q, k, v * 2, causal=True)
-    assert torch.equal(a.float() * 2, b.float())
+    G.assert_doubled_exactly(a, b)
 
 
 # ----------------------------------------------------------------------------- paged

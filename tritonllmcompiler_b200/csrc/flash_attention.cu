@@ -93,6 +93,11 @@ struct Args {
   int vec_store;
 };
 
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[32]) { tmem_ld32(taddr, r); }
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[16]) { tmem_ld16(taddr, r); }
+__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t (&r)[32]) { tmem_st32(taddr, r); }
+__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t (&r)[16]) { tmem_st16(taddr, r); }
+
 // K-major operand (Q or K): k16 step `k` of the D reduction.
 template <int D>
 __device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int k) {
@@ -109,6 +114,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                      const __grid_constant__ CUtensorMap tm_v, const Args a) {
   using G = Geo<D>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr int OC = D < 32 ? D : 32;  // O columns moved per TMEM load/store
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -320,13 +326,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       l_run = l_run * alpha + psum;
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+        // O row *= alpha, OC columns at a time (OC = 16 for D = 16, else 32).
 #pragma unroll 1
-        for (int c = 0; c < D; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(tmem_base + lane_off + O_COL + c, r);
+        for (int c = 0; c < D; c += OC) {
+          uint32_t r[OC];
+          tmem_ld_cols(tmem_base + lane_off + O_COL + c, r);
 #pragma unroll
-          for (int t = 0; t < 32; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * alpha);
-          tmem_st32(tmem_base + lane_off + O_COL + c, r);
+          for (int t = 0; t < OC; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * alpha);
+          tmem_st_cols(tmem_base + lane_off + O_COL + c, r);
         }
       }
       m_run = mx;
@@ -342,13 +349,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float inv_l = 1.0f / l_run;
       T *orow = static_cast<T *>(a.o) + b * a.so0 + h * a.so1 + static_cast<int64_t>(qg) * a.so2;
 #pragma unroll 1
-      for (int c = 0; c < D; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(tmem_base + lane_off + O_COL + c, r);
+      for (int c = 0; c < D; c += OC) {
+        uint32_t r[OC];
+        tmem_ld_cols(tmem_base + lane_off + O_COL + c, r);
         if (qg < a.Sq) {
           if (a.vec_store) {
 #pragma unroll
-            for (int t = 0; t < 32; t += 8) {
+            for (int t = 0; t < OC; t += 8) {
               uint4 pk;
               pk.x = Pack2<T>::pack(__uint_as_float(r[t + 0]) * inv_l, __uint_as_float(r[t + 1]) * inv_l);
               pk.y = Pack2<T>::pack(__uint_as_float(r[t + 2]) * inv_l, __uint_as_float(r[t + 3]) * inv_l);
@@ -358,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           } else {
 #pragma unroll
-            for (int t = 0; t < 32; ++t) orow[(c + t) * a.so3] = from_f32<T>(__uint_as_float(r[t]) * inv_l);
+            for (int t = 0; t < OC; ++t) orow[(c + t) * a.so3] = from_f32<T>(__uint_as_float(r[t]) * inv_l);
           }
         }
       }

@@ -366,7 +366,9 @@ extern "C" int tllm_swiglu(const void *x, const void *w1, const void *w3, void *
                  dtype);
   TLLM_CHECK_ARG(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31), "swiglu: dimension too large");
   if (M == 0 || N == 0) return TLLM_OK;
-  TLLM_CHECK_ARG(x && w1 && w3 && out, "swiglu: null tensor pointer");
+  TLLM_CHECK_ARG(out, "swiglu: null output pointer");
+  // With K == 0 the inputs are empty (and may be null); the result is silu(0) * 0 = 0.
+  TLLM_CHECK_ARG(K == 0 || (x && w1 && w3), "swiglu: null tensor pointer");
   TLLM_CHECK_ARG(lda >= K && ldb1 >= N && ldb3 >= N && ldo >= N, "swiglu: leading dimension too small");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (K == 0) {

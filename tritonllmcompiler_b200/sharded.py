@@ -1,0 +1,149 @@
+"""Multi-GPU partitioning of the four-op hot path (one process per GPU, torch.distributed).
+
+The reference is single-GPU only. Across the GPUs of one node the operators shard as:
+
+* flash_attention over heads: rank r owns heads [r*H/g, (r+1)*H/g) of q/k/v/o; no
+  communication (``head_range``, ``flash_attention_head_sharded``).
+* paged_attention over sequences: each rank owns whole sequences, their block-table rows and
+  only their physical blocks, re-indexed into a rank-local pool; no communication
+  (``partition_sequences``, ``localize_blocks``). Sequences are balanced by token count
+  (greedy longest-first) because context lengths vary widely.
+* swiglu over output columns: rank r holds x and the column slices w1[:, Nr], w3[:, Nr],
+  computes out[:, Nr], and the slices are all-gathered over NVLink with NCCL
+  (``swiglu_column_sharded``). Row chunks let the gather of chunk c overlap the GEMM of
+  chunk c+1 on a second stream.
+
+The per-rank compute function is a parameter only so the partitioning and gather logic can
+be exercised on CPU ranks (gloo); the default is the CUDA operator.
+"""
+from __future__ import annotations
+
+from typing import Callable, Sequence
+
+import torch
+import torch.distributed as dist
+
+
+def head_range(num_heads: int, rank: int, world: int) -> tuple[int, int]:
+    """Heads [h0, h1) owned by `rank`; num_heads must divide evenly."""
+    if num_heads % world:
+        raise ValueError(f"{num_heads} heads do not split over {world} ranks")
+    per = num_heads // world
+    return rank * per, (rank + 1) * per
+
+
+def flash_attention_head_sharded(q_local, k_local, v_local, *, causal=False, sm_scale=None,
+                                 op: Callable | None = None):
+    """Attention over this rank's heads (inputs and output stay sharded)."""
+    if op is None:
+        from tritonllmcompiler_b200.ops.flash_attention import flash_attention as op
+    return op(q_local, k_local, v_local, causal=causal, sm_scale=sm_scale)
+
+
+def partition_sequences(context_lens: Sequence[int], world: int, scheme: str = "tokens") -> list[list[int]]:
+    """Assigns sequence indices to ranks.
+
+    scheme="count": contiguous runs of ceil(B/world) sequences.
+    scheme="tokens": greedy longest-first onto the rank with the fewest tokens so far
+    (ties broken by rank), each rank's list sorted ascending.
+    """
+    lens = [int(x) for x in context_lens]
+    b = len(lens)
+    if scheme == "count":
+        per = -(-b // world) if b else 0
+        return [list(range(r * per, min(b, (r + 1) * per))) for r in range(world)]
+    if scheme != "tokens":
+        raise ValueError(f"unknown scheme {scheme!r}")
+    load = [0] * world
+    out: list[list[int]] = [[] for _ in range(world)]
+    for i in sorted(range(b), key=lambda i: (-lens[i], i)):
+        r = min(range(world), key=lambda r: (load[r], r))
+        out[r].append(i)
+        load[r] += lens[i]
+    return [sorted(x) for x in out]
+
+
+def localize_blocks(block_tables: torch.Tensor, context_lens: torch.Tensor, seq_ids: Sequence[int],
+                    block_size: int):
+    """Rank-local view of a paged KV cache for the sequences `seq_ids`.
+
+    Returns (global_block_ids, local_tables, local_lens): the physical blocks the sequences
+    use (in first-use order; gather k_cache[global_block_ids] to build the local pool), the
+    block tables re-indexed into that local pool (padding entries 0), and their lengths.
+    Only the first ceil(len/block_size) entries of a row are read, as the reference does.
+    """
+    bt = block_tables.cpu()
+    cl = context_lens.cpu()
+    ids: list[int] = []
+    remap: dict[int, int] = {}
+    rows = []
+    width = 1
+    for s in seq_ids:
+        n = (int(cl[s]) + block_size - 1) // block_size
+        n = min(n, bt.shape[1])
+        row = []
+        for j in range(n):
+            g = int(bt[s, j])
+            if g not in remap:
+                remap[g] = len(ids)
+                ids.append(g)
+            row.append(remap[g])
+        rows.append(row)
+        width = max(width, len(row))
+    local = torch.zeros(len(seq_ids), width, dtype=torch.int32)
+    for i, row in enumerate(rows):
+        if row:
+            local[i, :len(row)] = torch.tensor(row, dtype=torch.int32)
+    lens = torch.tensor([int(cl[s]) for s in seq_ids], dtype=torch.int32)
+    return torch.tensor(ids, dtype=torch.int64), local, lens
+
+
+def column_range(n: int, rank: int, world: int, align: int = 8) -> tuple[int, int]:
+    """Output columns [n0, n1) of `rank`; each slice is a multiple of `align` columns."""
+    if n % (world * align):
+        raise ValueError(f"N={n} does not split into {world} slices of a multiple of {align}")
+    per = n // world
+    return rank * per, (rank + 1) * per
+
+
+def swiglu_column_sharded(x: torch.Tensor, w1_local: torch.Tensor, w3_local: torch.Tensor,
+                          group=None, *, chunks: int = 1, op: Callable | None = None,
+                          out: torch.Tensor | None = None) -> torch.Tensor:
+    """out = silu(x @ w1) * (x @ w3) with w1/w3 column-sharded over the process group.
+
+    Every rank passes the full x [M, K] and its column slices [K, N/g]; every rank returns
+    the full [M, N] output. With chunks > 1 the rows are processed in `chunks` blocks and
+    the all-gather of block c runs on a side stream (CUDA) while block c+1 computes.
+    """
+    if op is None:
+        from tritonllmcompiler_b200.ops.swiglu import swiglu as op
+    world = dist.get_world_size(group)
+    m = x.shape[0]
+    n_loc = w1_local.shape[1]
+    n = n_loc * world
+    if out is None:
+        out = torch.empty((m, n), dtype=x.dtype, device=x.device)
+    bounds = [(m * c) // chunks for c in range(chunks + 1)]
+    cuda = x.is_cuda
+    comm = torch.cuda.Stream(device=x.device) if (cuda and chunks > 1) else None
+    pending = []
+    for c in range(chunks):
+        r0, r1 = bounds[c], bounds[c + 1]
+        if r1 == r0:
+            continue
+        part = op(x[r0:r1], w1_local, w3_local)
+        gathered = torch.empty((world, r1 - r0, n_loc), dtype=x.dtype, device=x.device)
+        if comm is not None:
+            comm.wait_stream(torch.cuda.current_stream(x.device))
+            with torch.cuda.stream(comm):
+                dist.all_gather_into_tensor(gathered.view(-1), part.contiguous().view(-1), group=group)
+                out[r0:r1].view(r1 - r0, world, n_loc).copy_(gathered.permute(1, 0, 2))
+            part.record_stream(comm)
+            gathered.record_stream(comm)
+            pending.append(gathered)
+        else:
+            dist.all_gather_into_tensor(gathered.view(-1), part.contiguous().view(-1), group=group)
+            out[r0:r1].view(r1 - r0, world, n_loc).copy_(gathered.permute(1, 0, 2))
+    if comm is not None:
+        torch.cuda.current_stream(x.device).wait_stream(comm)
+    return out
