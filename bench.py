@@ -415,7 +415,7 @@ def run_ours(args):
     k_ms = sum(kt) / len(kt)
     k_flops = 4.0 * M * K * n_loc
     achieved = k_flops / (k_ms * 1e-3) / 1e12
-    traffic = profile_traffic("swiglu_m4096_k4096_n14336_fp16.md") if world == 1 else None
+    traffic = profile_traffic("swiglu_tc_kernel_m4096_k4096_n14336_fp16.md") if world == 1 else None
 
     # End to end through the public API with pinned host buffers (H2D inputs, D2H result).
     hx = x.cpu().pin_memory()

@@ -49,6 +49,13 @@ TLLM_API const char *tllm_last_error(void);
  * Synchronises the current device (a debugging aid, not part of the hot path). */
 TLLM_API int tllm_debug_status(int *out);
 
+/* Failure-detection self-test: enqueues a one-warp kernel that waits on an mbarrier nothing
+ * arrives on. The bounded wait gives up after about 10 ms and records 0x17F
+ * (TLLM_DEV_WAIT_TIMEOUT + 0x7F), which tllm_debug_status then returns; the context stays
+ * usable. No counterpart in the reference (its CUDA helper exits the process on errors,
+ * common/cuda_utils.cuh:10-18). */
+TLLM_API int tllm_selftest_bounded_wait(void *stream);
+
 /*
  * FlashAttention forward: o = softmax(q k^T * sm_scale [+ causal mask]) v per (b, h).
  * Replaces flash_attention() in python/triton_llm/ops/flash_attention.py:107-133 and its
@@ -62,6 +69,15 @@ TLLM_API int tllm_flash_attn_fwd(const void *q, const void *k, const void *v, vo
                         const int64_t *sq, const int64_t *sk, const int64_t *sv,
                         const int64_t *so, float sm_scale, int causal, int dtype,
                         void *stream);
+
+/* Same as tllm_flash_attn_fwd with an explicit kernel choice, for cross-checking the two
+ * implementations against each other: variant 0 = two 128-row query tiles per CTA with
+ * ping-pong softmax warpgroups (the default), 1 = one query tile per CTA. */
+TLLM_API int tllm_flash_attn_fwd_variant(const void *q, const void *k, const void *v, void *o,
+                                int64_t B, int64_t H, int64_t Sq, int64_t Sk, int64_t D,
+                                const int64_t *sq, const int64_t *sk, const int64_t *sv,
+                                const int64_t *so, float sm_scale, int causal, int dtype,
+                                int variant, void *stream);
 
 /*
  * Bytes of device workspace tllm_paged_attn_decode needs for this problem (the split-KV

@@ -24,10 +24,16 @@ SIGNATURES = {
     "tllm_version": (ctypes.c_char_p, []),
     "tllm_last_error": (ctypes.c_char_p, []),
     "tllm_debug_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "tllm_selftest_bounded_wait": (ctypes.c_int, [_vp]),
     "tllm_flash_attn_fwd": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _c_i64p, _c_i64p, _c_i64p, _c_i64p,
          ctypes.c_float, ctypes.c_int, ctypes.c_int, _vp],
+    ),
+    "tllm_flash_attn_fwd_variant": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _c_i64p, _c_i64p, _c_i64p, _c_i64p,
+         ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp],
     ),
     "tllm_paged_attn_workspace_size": (ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64]),
     "tllm_paged_attn_decode": (

@@ -384,12 +384,362 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// =======================================================================================
+// Ping-pong kernel: one CTA owns two adjacent 128-row query tiles X = 0 (rows [256t, +128))
+// and X = 1 (the next 128 rows) of one (b, h), sharing every K/V tile.
+//   warp 0        TMA producer (both Q tiles once, K_j and V_j through 2-slot rings)
+//   warp 1        TMEM allocation + UMMA issue
+//   warps 4-7     softmax for tile 0, warps 8-11 softmax for tile 1 (one query row each)
+// TMEM (512 columns): S_X at [128X, 128X+128), O_X at [256+128X, 256+128X+D). After the
+// softmax of tile X has read S_X(j) it overwrites S_X's first 64 columns with P_X(j) (fp16/
+// bf16 pairs), and O_X += P_X V_j is issued with A read from TMEM. Per tile the MMAs run
+// QK(j) -> PV(j) -> QK(j+1) in issue order, so S/P reuse needs no extra barrier, while the
+// tensor core alternates between the two tiles: the softmax of one tile overlaps the MMAs
+// of the other. O is rescaled lazily: the running max used for the exponentials only moves
+// when a row's max grows by more than kLazyRescaleLog2 (so P stays below 2^8), which makes
+// in-TMEM rescaling rare after the first key tiles.
+// =======================================================================================
+constexpr int kPPThreads = 384;
+constexpr int kPPSoftmaxWarp0 = 4;
+constexpr float kLazyRescaleLog2 = 8.0f;
+
+template <int D>
+struct GeoPP {
+  static constexpr int SWB = Geo<D>::SWB;
+  static constexpr int CHUNKS = Geo<D>::CHUNKS;
+  static constexpr int CHUNK_BYTES = Geo<D>::CHUNK_BYTES;
+  static constexpr int TILE_BYTES = Geo<D>::TILE_BYTES;
+  static constexpr uint32_t LAYOUT = Geo<D>::LAYOUT;
+  static constexpr int Q_OFF = 0;                       // two Q tiles
+  static constexpr int K_OFF = Q_OFF + 2 * TILE_BYTES;  // two K slots
+  static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;  // two V slots
+  static constexpr int BAR_OFF = V_OFF + 2 * TILE_BYTES;
+  static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+};
+
+enum : int { SITE_PFULL = 9, SITE_ODONE = 10 };
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kPPThreads, 1)
+    flash_pp_kernel(const __grid_constant__ CUtensorMap tm_q,
+                    const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const Args a) {
+  using G = GeoPP<D>;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr int OC = D < 32 ? D : 32;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + G::BAR_OFF);
+  uint64_t *q_full = bars + 0;
+  uint64_t *k_full = bars + 1;   // [2]
+  uint64_t *k_empty = bars + 3;  // [2]
+  uint64_t *v_full = bars + 5;   // [2]
+  uint64_t *v_empty = bars + 7;  // [2]
+  uint64_t *s_full = bars + 9;   // [2] per tile
+  uint64_t *p_full = bars + 11;  // [2] per tile
+  uint64_t *o_done = bars + 13;  // [2] per tile
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 15);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int bh = blockIdx.x;
+  const int b = bh / a.H;
+  const int h = bh % a.H;
+  const int n_pairs = (a.n_qtiles + 1) / 2;
+  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.y);  // heaviest causal pairs first
+  const int q0 = pair * 2 * BM;
+  const int kv_tiles_all = (a.Sk + BN - 1) / BN;
+  int nkv[2];
+#pragma unroll
+  for (int X = 0; X < 2; ++X) {
+    const int qx0 = q0 + X * BM;
+    int n = qx0 < a.Sq ? kv_tiles_all : 0;
+    if (a.causal && n > 0) n = min(n, (min(qx0 + BM, a.Sq) - 1) / BN + 1);
+    nkv[X] = n;
+  }
+  const int n_kv = max(nkv[0], nkv[1]);
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(q_full), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&k_full[s]), 1);
+      mbar_init(smem_u32(&k_empty[s]), 1);
+      mbar_init(smem_u32(&v_full[s]), 1);
+      mbar_init(smem_u32(&v_empty[s]), 1);
+      mbar_init(smem_u32(&s_full[s]), 1);
+      mbar_init(smem_u32(&p_full[s]), kSoftmaxThreads);
+      mbar_init(smem_u32(&o_done[s]), 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const uint32_t sQ = smem_u32(smem + G::Q_OFF);
+  const uint32_t sK = smem_u32(smem + G::K_OFF);
+  const uint32_t sV = smem_u32(smem + G::V_OFF);
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0 && n_kv > 0) {
+      const uint32_t qb = smem_u32(q_full);
+      mbar_arrive_expect_tx(qb, G::TILE_BYTES * ((nkv[0] > 0) + (nkv[1] > 0)));
+#pragma unroll
+      for (int X = 0; X < 2; ++X) {
+        if (nkv[X] == 0) continue;
+#pragma unroll
+        for (int c = 0; c < G::CHUNKS; ++c)
+          tma_load_4d(sQ + X * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_q, qb, c * (G::SWB / 2),
+                      q0 + X * BM, h, b);
+      }
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j & 1;
+        const uint32_t par = ((j >> 1) & 1) ^ 1;
+        if (!mbar_wait(smem_u32(&k_empty[s]), par, abort_flag, &g_flash_status,
+                       TLLM_DEV_WAIT_TIMEOUT + SITE_KEMPTY))
+          break;
+        const uint32_t kb = smem_u32(&k_full[s]);
+        mbar_arrive_expect_tx(kb, G::TILE_BYTES);
+#pragma unroll
+        for (int c = 0; c < G::CHUNKS; ++c)
+          tma_load_4d(sK + s * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_k, kb, c * (G::SWB / 2),
+                      j * BN, h, b);
+        if (!mbar_wait(smem_u32(&v_empty[s]), par, abort_flag, &g_flash_status,
+                       TLLM_DEV_WAIT_TIMEOUT + SITE_VEMPTY))
+          break;
+        const uint32_t vb = smem_u32(&v_full[s]);
+        mbar_arrive_expect_tx(vb, G::TILE_BYTES);
+#pragma unroll
+        for (int c = 0; c < G::CHUNKS; ++c)
+          tma_load_4d(sV + s * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_v, vb, c * (G::SWB / 2),
+                      j * BN, h, b);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ UMMA issuer -------------------------------
+    if (lane == 0 && n_kv > 0) {
+      const uint32_t idesc_qk = make_idesc_f16(BM, BN, kBF16, false, false);
+      const uint32_t idesc_pv = make_idesc_f16(BM, D, kBF16, false, true);
+      auto issue_qk = [&](int X, int j) {
+        const uint32_t kbase = sK + (j & 1) * G::TILE_BYTES;
+        const uint32_t qbase = sQ + X * G::TILE_BYTES;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k)
+          umma_f16_ss(tmem_base + X * BN, kmajor_desc<D>(qbase, k), kmajor_desc<D>(kbase, k),
+                      idesc_qk, k != 0 ? 1u : 0u);
+        umma_commit(smem_u32(&s_full[X]));
+      };
+      bool ok = mbar_wait(smem_u32(q_full), 0, abort_flag, &g_flash_status,
+                          TLLM_DEV_WAIT_TIMEOUT + SITE_Q) &&
+                mbar_wait(smem_u32(&k_full[0]), 0, abort_flag, &g_flash_status,
+                          TLLM_DEV_WAIT_TIMEOUT + SITE_KFULL);
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int X = 0; X < 2; ++X)
+          if (nkv[X] > 0) issue_qk(X, 0);
+        umma_commit(smem_u32(&k_empty[0]));
+      }
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(smem_u32(&v_full[s]), (j >> 1) & 1, abort_flag, &g_flash_status,
+                       TLLM_DEV_WAIT_TIMEOUT + SITE_VFULL)) {
+          ok = false;
+          break;
+        }
+        const uint32_t vbase = sV + s * G::TILE_BYTES;
+        bool next_k_ready = false;
+#pragma unroll
+        for (int X = 0; X < 2; ++X) {
+          if (j >= nkv[X]) continue;
+          if (!mbar_wait(smem_u32(&p_full[X]), j & 1, abort_flag, &g_flash_status,
+                         TLLM_DEV_WAIT_TIMEOUT + SITE_PFULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t p_tmem = tmem_base + X * BN;
+          const uint32_t o_tmem = tmem_base + O_COL + X * BN;
+#pragma unroll
+          for (int k = 0; k < BN / 16; ++k) {
+            const uint64_t bdesc =
+                make_sdesc(vbase + k * 16 * G::SWB, G::CHUNK_BYTES, 8 * G::SWB, G::LAYOUT);
+            umma_f16_ts(o_tmem, p_tmem + k * 8, bdesc, idesc_pv, (j | k) != 0 ? 1u : 0u);
+          }
+          if (j == nkv[X] - 1) {
+            umma_commit(smem_u32(&o_done[X]));
+          } else {
+            if (!next_k_ready) {
+              if (!mbar_wait(smem_u32(&k_full[(j + 1) & 1]), ((j + 1) >> 1) & 1, abort_flag,
+                             &g_flash_status, TLLM_DEV_WAIT_TIMEOUT + SITE_KFULL)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              next_k_ready = true;
+            }
+            issue_qk(X, j + 1);
+          }
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(&v_empty[s]));
+        if (next_k_ready) umma_commit(smem_u32(&k_empty[(j + 1) & 1]));
+      }
+    }
+  } else if (warp >= kPPSoftmaxWarp0) {
+    // ------------------------------ softmax / epilogue ------------------------
+    const int X = (warp - kPPSoftmaxWarp0) >> 2;
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const int qx0 = q0 + X * BM;
+    const int qg = qx0 + row;
+    const int nk = nkv[X];
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t s_tm = tmem_base + lane_off + X * BN;
+    const uint32_t o_tm = tmem_base + lane_off + O_COL + X * BN;
+    float m_use = -INFINITY;  // max the exponentials are taken against (lazily updated)
+    float l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nk; ++j) {
+      if (!mbar_wait(smem_u32(&s_full[X]), j & 1, abort_flag, &g_flash_status,
+                     TLLM_DEV_WAIT_TIMEOUT + SITE_SFULL)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int k0 = j * BN;
+      const bool need_mask = (k0 + BN > a.Sk) || (a.causal && k0 + BN - 1 > qx0);
+      // Pass 1: row max of the scaled, masked scores.
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(s_tm + c, r);
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          float v = __uint_as_float(r[t]) * a.scale_log2;
+          if (need_mask) {
+            const int kg = k0 + c + t;
+            if (kg >= a.Sk || (a.causal && kg > qg)) v = -INFINITY;
+          }
+          mx = fmaxf(mx, v);
+        }
+      }
+      float alpha = 1.0f;
+      bool rescale = false;
+      if (m_use == -INFINITY) {
+        m_use = mx;  // first tile: O not written yet, nothing to rescale
+      } else if (mx > m_use + kLazyRescaleLog2) {
+        alpha = exp2f(m_use - mx);
+        m_use = mx;
+        rescale = true;
+      }
+      const float m_exp = m_use == -INFINITY ? 0.f : m_use;
+      // Pass 2: P = exp2(s - m) written over S's first 64 columns as packed pairs.
+      float psum = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(s_tm + c, r);
+        uint32_t pk[16];
+#pragma unroll
+        for (int t = 0; t < 32; t += 2) {
+          float v0 = __uint_as_float(r[t]) * a.scale_log2;
+          float v1 = __uint_as_float(r[t + 1]) * a.scale_log2;
+          if (need_mask) {
+            const int kg = k0 + c + t;
+            if (kg >= a.Sk || (a.causal && kg > qg)) v0 = -INFINITY;
+            if (kg + 1 >= a.Sk || (a.causal && kg + 1 > qg)) v1 = -INFINITY;
+          }
+          const float p0 = exp2f(v0 - m_exp);
+          const float p1 = exp2f(v1 - m_exp);
+          psum += p0 + p1;
+          pk[t >> 1] = Pack2<T>::pack(p0, p1);
+        }
+        tmem_st16(s_tm + (c >> 1), pk);
+      }
+      l_run = l_run * alpha + psum;
+      // O_X is stable here: PV_X(j-1) was issued before QK_X(j), whose completion s_full
+      // signalled.
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+        for (int c = 0; c < D; c += OC) {
+          uint32_t r[OC];
+          tmem_ld_cols(o_tm + c, r);
+#pragma unroll
+          for (int t = 0; t < OC; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * alpha);
+          tmem_st_cols(o_tm + c, r);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&p_full[X]));
+    }
+    // ---- epilogue: O / l -> global ----
+    if (ok && nk > 0 &&
+        mbar_wait(smem_u32(&o_done[X]), 0, abort_flag, &g_flash_status,
+                  TLLM_DEV_WAIT_TIMEOUT + SITE_ODONE)) {
+      tc_fence_after();
+      const float inv_l = 1.0f / l_run;
+      T *orow = static_cast<T *>(a.o) + b * a.so0 + h * a.so1 + static_cast<int64_t>(qg) * a.so2;
+#pragma unroll 1
+      for (int c = 0; c < D; c += OC) {
+        uint32_t r[OC];
+        tmem_ld_cols(o_tm + c, r);
+        if (qg < a.Sq) {
+          if (a.vec_store) {
+#pragma unroll
+            for (int t = 0; t < OC; t += 8) {
+              uint4 pk;
+              pk.x = Pack2<T>::pack(__uint_as_float(r[t + 0]) * inv_l, __uint_as_float(r[t + 1]) * inv_l);
+              pk.y = Pack2<T>::pack(__uint_as_float(r[t + 2]) * inv_l, __uint_as_float(r[t + 3]) * inv_l);
+              pk.z = Pack2<T>::pack(__uint_as_float(r[t + 4]) * inv_l, __uint_as_float(r[t + 5]) * inv_l);
+              pk.w = Pack2<T>::pack(__uint_as_float(r[t + 6]) * inv_l, __uint_as_float(r[t + 7]) * inv_l);
+              *reinterpret_cast<uint4 *>(orow + c + t) = pk;
+            }
+          } else {
+#pragma unroll
+            for (int t = 0; t < OC; ++t)
+              orow[(c + t) * a.so3] = from_f32<T>(__uint_as_float(r[t]) * inv_l);
+          }
+        }
+      }
+    } else if (nk == 0 && qx0 < a.Sq && qg < a.Sq) {
+      // No keys at all (Sk == 0): 0/0, as in the reference.
+      T *orow = static_cast<T *>(a.o) + b * a.so0 + h * a.so1 + static_cast<int64_t>(qg) * a.so2;
+      for (int c = 0; c < D; ++c) orow[c * a.so3] = from_f32<T>(NAN);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Kernel variants: the two-tile ping-pong kernel is the default; the single-tile kernel is
+// kept as a cross-check (tllm_flash_attn_fwd_variant).
+constexpr int kVariantPingPong = 0;
+constexpr int kVariantSingleTile = 1;
 
 template <typename T, int D>
 int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, int64_t H,
              int64_t Sq, int64_t Sk, const int64_t *sq, const int64_t *sk, const int64_t *sv,
-             const int64_t *so, float sm_scale, int causal, cudaStream_t st) {
+             const int64_t *so, float sm_scale, int causal, int variant, cudaStream_t st) {
   using G = Geo<D>;
   const CUtensorMapDataType dt = std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                                  : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -426,23 +776,32 @@ int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, in
   a.scale_log2 = sm_scale * kLog2e;
   a.causal = causal ? 1 : 0;
   a.vec_store = (so[3] == 1 && so[0] % 8 == 0 && so[1] % 8 == 0 && so[2] % 8 == 0 && aligned16(o)) ? 1 : 0;
-  auto kern = flash_fwd_kernel<T, D>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
-  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(flash)");
-  dim3 grid(static_cast<unsigned>(B * H), static_cast<unsigned>(a.n_qtiles));
-  kern<<<grid, kThreads, G::SMEM_BYTES, st>>>(mq, mk, mv, a);
-  return cuda_status(cudaGetLastError(), "flash launch");
+  if (variant == kVariantSingleTile) {
+    auto kern = flash_fwd_kernel<T, D>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(flash)");
+    dim3 grid(static_cast<unsigned>(B * H), static_cast<unsigned>(a.n_qtiles));
+    kern<<<grid, kThreads, G::SMEM_BYTES, st>>>(mq, mk, mv, a);
+    return cuda_status(cudaGetLastError(), "flash launch");
+  }
+  using GP = GeoPP<D>;
+  auto kern = flash_pp_kernel<T, D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GP::SMEM_BYTES);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(flash pp)");
+  dim3 grid(static_cast<unsigned>(B * H), static_cast<unsigned>((a.n_qtiles + 1) / 2));
+  kern<<<grid, kPPThreads, GP::SMEM_BYTES, st>>>(mq, mk, mv, a);
+  return cuda_status(cudaGetLastError(), "flash pp launch");
 }
 
 template <typename T>
 int launch(const void *q, const void *k, const void *v, void *o, int64_t B, int64_t H, int64_t Sq,
            int64_t Sk, int64_t D, const int64_t *sq, const int64_t *sk, const int64_t *sv,
-           const int64_t *so, float sm_scale, int causal, cudaStream_t st) {
+           const int64_t *so, float sm_scale, int causal, int variant, cudaStream_t st) {
   switch (D) {
-    case 16: return launch_d<T, 16>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, st);
-    case 32: return launch_d<T, 32>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, st);
-    case 64: return launch_d<T, 64>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, st);
-    default: return launch_d<T, 128>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, st);
+    case 16: return launch_d<T, 16>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st);
+    case 32: return launch_d<T, 32>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st);
+    case 64: return launch_d<T, 64>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st);
+    default: return launch_d<T, 128>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st);
   }
 }
 
@@ -450,18 +809,21 @@ int launch(const void *q, const void *k, const void *v, void *o, int64_t B, int6
 }  // namespace flash
 }  // namespace tllm
 
-extern "C" int tllm_flash_attn_fwd(const void *q, const void *k, const void *v, void *o,
-                                   int64_t B, int64_t H, int64_t Sq, int64_t Sk, int64_t D,
-                                   const int64_t *sq, const int64_t *sk, const int64_t *sv,
-                                   const int64_t *so, float sm_scale, int causal, int dtype,
-                                   void *stream) {
-  using namespace tllm;
+namespace tllm {
+namespace flash {
+namespace {
+
+int entry(const void *q, const void *k, const void *v, void *o, int64_t B, int64_t H, int64_t Sq,
+          int64_t Sk, int64_t D, const int64_t *sq, const int64_t *sk, const int64_t *sv,
+          const int64_t *so, float sm_scale, int causal, int dtype, int variant, void *stream) {
   clear_error();
   TLLM_CHECK_ARG(B >= 0 && H >= 0 && Sq >= 0 && Sk >= 0, "flash_attention: negative dimension");
   TLLM_CHECK_ARG(D == 16 || D == 32 || D == 64 || D == 128,
                  "flash_attention: head dim %lld not in {16,32,64,128}", (long long)D);
   TLLM_CHECK_ARG(dtype == TLLM_DTYPE_F16 || dtype == TLLM_DTYPE_BF16,
                  "flash_attention: unsupported dtype %d", dtype);
+  TLLM_CHECK_ARG(variant == kVariantPingPong || variant == kVariantSingleTile,
+                 "flash_attention: unknown kernel variant %d", variant);
   TLLM_CHECK_ARG(sq && sk && sv && so, "flash_attention: null stride array");
   if (B == 0 || H == 0 || Sq == 0) return TLLM_OK;
   TLLM_CHECK_ARG(q && k && v && o, "flash_attention: null tensor pointer");
@@ -473,11 +835,33 @@ extern "C" int tllm_flash_attn_fwd(const void *q, const void *k, const void *v, 
   for (int i = 0; i < 3; ++i)
     TLLM_CHECK_ARG(sq[i] % 8 == 0 && sk[i] % 8 == 0 && sv[i] % 8 == 0,
                    "flash_attention: q/k/v strides must be multiples of 8 elements");
-  TLLM_CHECK_ARG(flash::aligned16(q) && flash::aligned16(k) && flash::aligned16(v),
+  TLLM_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v),
                  "flash_attention: q/k/v must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == TLLM_DTYPE_F16)
-    return flash::launch<__half>(q, k, v, o, B, H, Sq, Sk, D, sq, sk, sv, so, sm_scale, causal, st);
-  return flash::launch<__nv_bfloat16>(q, k, v, o, B, H, Sq, Sk, D, sq, sk, sv, so, sm_scale, causal,
-                                      st);
+    return launch<__half>(q, k, v, o, B, H, Sq, Sk, D, sq, sk, sv, so, sm_scale, causal, variant, st);
+  return launch<__nv_bfloat16>(q, k, v, o, B, H, Sq, Sk, D, sq, sk, sv, so, sm_scale, causal,
+                               variant, st);
+}
+
+}  // namespace
+}  // namespace flash
+}  // namespace tllm
+
+extern "C" int tllm_flash_attn_fwd(const void *q, const void *k, const void *v, void *o,
+                                   int64_t B, int64_t H, int64_t Sq, int64_t Sk, int64_t D,
+                                   const int64_t *sq, const int64_t *sk, const int64_t *sv,
+                                   const int64_t *so, float sm_scale, int causal, int dtype,
+                                   void *stream) {
+  return tllm::flash::entry(q, k, v, o, B, H, Sq, Sk, D, sq, sk, sv, so, sm_scale, causal, dtype,
+                            tllm::flash::kVariantPingPong, stream);
+}
+
+extern "C" int tllm_flash_attn_fwd_variant(const void *q, const void *k, const void *v, void *o,
+                                           int64_t B, int64_t H, int64_t Sq, int64_t Sk,
+                                           int64_t D, const int64_t *sq, const int64_t *sk,
+                                           const int64_t *sv, const int64_t *so, float sm_scale,
+                                           int causal, int dtype, int variant, void *stream) {
+  return tllm::flash::entry(q, k, v, o, B, H, Sq, Sk, D, sq, sk, sv, so, sm_scale, causal, dtype,
+                            variant, stream);
 }
