@@ -110,6 +110,34 @@ TLLM_API int tllm_paged_attn_decode(const void *q, const void *k_cache, const vo
                            const int64_t *sbt, const int64_t *so, float sm_scale,
                            int dtype, void *stream);
 
+/* Size of the fixed device array tllm_paged_attn_decode_noalloc keeps its split-KV
+ * partials in (32 MiB per GPU that loads the library). */
+#define TLLM_PAGED_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/*
+ * Same operation as tllm_paged_attn_decode, for callers that cannot allocate device memory
+ * (engines that reserve all device memory at start-up and forbid later cudaMalloc, or
+ * foreign-language hosts without a device allocator). It has no counterpart in the
+ * reference. It allocates nothing: the split-KV partials go to a fixed array inside the
+ * library of TLLM_PAGED_NOALLOC_SCRATCH_BYTES bytes; a problem whose partials need more
+ * (tllm_paged_attn_workspace_size above that limit) is rejected with TLLM_ERR_WORKSPACE and
+ * nothing is launched. The caller still provides every input and the output.
+ *   - The first call on a device looks up the array's device address (once per device, with
+ *     that device current); make that first call before any stream capture.
+ *   - All calls share the one array and it keeps the last call's contents. Calls whose
+ *     kernels can overlap on the GPU (different streams, no ordering between them) race on
+ *     it and may return wrong results; order such calls on one stream or with events.
+ */
+TLLM_API int tllm_paged_attn_decode_noalloc(const void *q, const void *k_cache,
+                                   const void *v_cache, const int32_t *block_tables,
+                                   const int32_t *context_lens, void *o, int64_t B,
+                                   int64_t H, int64_t D, int64_t block_size,
+                                   int64_t max_blocks, int64_t num_blocks,
+                                   const int64_t *sq, const int64_t *skc,
+                                   const int64_t *svc, const int64_t *sbt,
+                                   const int64_t *so, float sm_scale, int dtype,
+                                   void *stream);
+
 /*
  * Fused RMSNorm + rotate-half RoPE:
  *   r = rsqrt(mean(x^2) + eps); y = round_to_dtype(x * r * w);

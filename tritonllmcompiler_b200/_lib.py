@@ -41,6 +41,11 @@ SIGNATURES = {
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _i64, _i64, _i64, _i64, _i64, _i64,
          _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, ctypes.c_float, ctypes.c_int, _vp],
     ),
+    "tllm_paged_attn_decode_noalloc": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
+         _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, ctypes.c_float, ctypes.c_int, _vp],
+    ),
     "tllm_rmsnorm_rope": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _c_i64p, _i64, _c_i64p, _c_i64p,

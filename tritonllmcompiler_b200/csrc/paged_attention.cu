@@ -16,6 +16,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <mutex>
+
 #include "common.h"
 #include "paged_attention.cuh"
 #include "ptx.cuh"
@@ -394,6 +396,107 @@ extern "C" int tllm_paged_attn_decode(const void *q, const void *k_cache, const 
                    "paged_attention: workspace must be 256-byte aligned");
     p.ws_ml = static_cast<float *>(workspace);
     p.ws_acc = reinterpret_cast<float *>(static_cast<char *>(workspace) + pl.ws_acc_offset);
+  }
+  return paged::run(p, dtype, static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free variant of the decode entry point.
+//
+// Some callers cannot hand this library a device workspace: engines that reserve all device
+// memory once at start-up and treat any later cudaMalloc as a fault (cudaMalloc can stall the
+// whole device and fragments a pre-planned pool), and foreign-language hosts that reach the
+// library through its C ABI with no device allocator of their own. For them the split-KV
+// partials live in the fixed array below instead of a caller-provided workspace. Every GPU
+// that loads this library keeps the array (TLLM_PAGED_NOALLOC_SCRATCH_BYTES) until the
+// process exits.
+// ---------------------------------------------------------------------------------------
+namespace tllm {
+namespace paged {
+namespace {
+
+__device__ __align__(256) unsigned char g_noalloc_scratch[TLLM_PAGED_NOALLOC_SCRATCH_BYTES];
+
+std::mutex g_noalloc_mutex;
+void *g_noalloc_ptr[64] = {};
+
+// Device address of g_noalloc_scratch on the current device. In host code the symbol name
+// only stands in for the device array, so the address is looked up once per device (with
+// that device current) and cached.
+int noalloc_scratch(void **out) {
+  int dev = -1;
+  TLLM_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(TLLM_ERR_CUDA, "paged_attention: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(paged no-alloc scratch)");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return TLLM_OK;
+}
+
+}  // namespace
+}  // namespace paged
+}  // namespace tllm
+
+extern "C" int tllm_paged_attn_decode_noalloc(const void *q, const void *k_cache,
+                                              const void *v_cache, const int32_t *block_tables,
+                                              const int32_t *context_lens, void *o, int64_t B,
+                                              int64_t H, int64_t D, int64_t block_size,
+                                              int64_t max_blocks, int64_t num_blocks,
+                                              const int64_t *sq, const int64_t *skc,
+                                              const int64_t *svc, const int64_t *sbt,
+                                              const int64_t *so, float sm_scale, int dtype,
+                                              void *stream) {
+  using namespace tllm;
+  clear_error();
+  TLLM_CHECK_ARG(dtype == TLLM_DTYPE_F16 || dtype == TLLM_DTYPE_BF16,
+                 "paged_attention_noalloc: unsupported dtype %d", dtype);
+  TLLM_CHECK_ARG(sq && skc && svc && sbt && so, "paged_attention_noalloc: null stride array");
+  TLLM_CHECK_ARG(max_blocks >= 0 && num_blocks >= 0, "paged_attention_noalloc: negative table size");
+  if (B == 0 || H == 0) return TLLM_OK;
+  TLLM_CHECK_ARG(q && k_cache && v_cache && block_tables && context_lens && o,
+                 "paged_attention_noalloc: null tensor pointer");
+  TLLM_CHECK_ARG(max_blocks >= 1, "paged_attention_noalloc: block_tables has no columns");
+  TLLM_CHECK_ARG(num_blocks >= 1, "paged_attention_noalloc: the caches hold no blocks");
+  TLLM_CHECK_ARG(max_blocks * block_size < (1LL << 31),
+                 "paged_attention_noalloc: max_blocks * block_size too large");
+  const Plan pl = paged::plan(B, H, D, block_size, max_blocks, sm_count());
+  if (pl.ws_bytes > TLLM_PAGED_NOALLOC_SCRATCH_BYTES)
+    return fail(TLLM_ERR_WORKSPACE,
+                "paged_attention_noalloc: this problem needs %zu bytes of split-KV scratch, more "
+                "than the library's fixed %zu-byte array; use tllm_paged_attn_decode with a "
+                "caller-provided workspace",
+                pl.ws_bytes, static_cast<size_t>(TLLM_PAGED_NOALLOC_SCRATCH_BYTES));
+  Params p{};
+  p.q = q; p.k_cache = k_cache; p.v_cache = v_cache;
+  p.block_tables = block_tables; p.context_lens = context_lens; p.o = o;
+  p.B = B; p.H = H; p.D = D;
+  p.num_blocks = num_blocks;
+  p.block_size = static_cast<int>(block_size);
+  p.log2_bs = block_size == 16 ? 4 : (block_size == 32 ? 5 : 6);
+  p.max_tokens = static_cast<int>(pl.max_tokens);
+  p.chunk = static_cast<int>(pl.chunk);
+  p.num_splits = static_cast<int>(pl.num_splits);
+  p.sq0 = sq[0]; p.sq1 = sq[1]; p.sq3 = sq[3];
+  p.skc0 = skc[0]; p.skc1 = skc[1]; p.skc2 = skc[2]; p.skc3 = skc[3];
+  p.svc0 = svc[0]; p.svc1 = svc[1]; p.svc2 = svc[2]; p.svc3 = svc[3];
+  p.sbt0 = sbt[0]; p.sbt1 = sbt[1];
+  p.so0 = so[0]; p.so1 = so[1]; p.so3 = so[3];
+  p.sm_scale = sm_scale;
+  int rc = paged::validate(p);
+  if (rc) return rc;
+  if (pl.num_splits > 1) {
+    // Every partial slot the merge kernel reads is written earlier in this same call, so the
+    // array needs no clearing between calls.
+    void *scratch = nullptr;
+    rc = paged::noalloc_scratch(&scratch);
+    if (rc) return rc;
+    p.ws_ml = static_cast<float *>(scratch);
+    p.ws_acc = reinterpret_cast<float *>(static_cast<char *>(scratch) + pl.ws_acc_offset);
   }
   return paged::run(p, dtype, static_cast<cudaStream_t>(stream));
 }
