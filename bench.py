@@ -44,6 +44,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-ops", action="store_true", help="skip the per-operator extras")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--chunks", type=int, default=1,
+                    help="N>1: row chunks whose all-gather overlaps the next chunk's GEMM")
     ap.add_argument("--op", choices=sorted(OP_CASES), default=None,
                     help="run only this operator case (steps+warmup launches) and print its timing")
     return ap.parse_args()
@@ -384,12 +386,14 @@ def run_ours(args):
     def kernel_only():
         return T.swiglu(x, w1l, w3l)
 
+    from tritonllmcompiler_b200 import sharded as S
+
+    out_full = torch.empty((M, N), dtype=torch.float16, device="cuda") if world > 1 else None
+
     def step():
-        out = T.swiglu(x, w1l, w3l)
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, out)
-            out = gathered.view(world, M, n_loc).permute(1, 0, 2).reshape(M, N)
-        return out
+        if world == 1:
+            return T.swiglu(x, w1l, w3l)
+        return S.swiglu_column_sharded(x, w1l, w3l, chunks=args.chunks, out=out_full)
 
     flops = 4.0 * M * K * N
     # Warm-up (also JIT-free: the library is prebuilt).
@@ -462,7 +466,8 @@ def run_ours(args):
             "data": "synthetic (seeded normal, x~N(0,1), w~N(0,1/K))",
             "config": {"workload": f"swiglu M{M} K{K} N{N} fp16 (Llama-3-8B MLP)",
                        "parallelism": "single GPU" if world == 1 else
-                       f"column-shard N over {world} ranks + NCCL all_gather_into_tensor + permute",
+                       f"column-shard N over {world} ranks + NCCL all_gather_into_tensor + "
+                       f"permute into [M, N] ({args.chunks} row chunk(s))",
                        "l2": "256 MiB buffer written between timed steps; inputs 267 MB > L2"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,

@@ -249,3 +249,22 @@ def test_paged_int64_metadata_and_strided_q(cuda_device):
     out = T.paged_attention(qs.cuda(), kc.cuda(), vc.cuda(), bt.long().cuda(), cl.long().cuda(), block_size=16)
     ref = O.paged_attention(_f32(q), _f32(kc), _f32(vc), bt.numpy(), cl.numpy(), block_size=16)
     _assert_close(out, ref)
+
+
+@pytest.mark.parametrize("b,h,s,d,causal", [(2, 4, 1000, 128, True), (1, 4, 384, 64, False),
+                                            (1, 2, 300, 32, True), (1, 2, 257, 16, False)])
+def test_flash_kernel_variants_agree(cuda_device, b, h, s, d, causal):
+    """The two-tile ping-pong kernel (default) and the single-tile kernel agree."""
+    from tritonllmcompiler_b200 import _lib
+
+    g = _gen(s + d)
+    q, k, v = (torch.randn(b, h, s, d, generator=g).half().cuda() for _ in range(3))
+    outs = []
+    for variant in (0, 1):
+        o = torch.empty_like(q)
+        _lib.check(_lib.load().tllm_flash_attn_fwd_variant(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), b, h, s, s, d,
+            _lib.strides(q), _lib.strides(k), _lib.strides(v), _lib.strides(o),
+            d ** -0.5, int(causal), 0, variant, torch.cuda.current_stream().cuda_stream))
+        outs.append(o)
+    assert torch.allclose(outs[0].float(), outs[1].float(), **G.tol(torch.float16))

@@ -132,10 +132,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int bh = blockIdx.x;
+  // 1-D grid, head-major: the query tiles of one (b, h) are adjacent in launch order (so the
+  // CTAs resident at any time share few heads' K/V in L2), heaviest causal tiles first.
+  const int bh = static_cast<int>(blockIdx.x / a.n_qtiles);
   const int b = bh / a.H;
   const int h = bh % a.H;
-  const int qt = a.n_qtiles - 1 - static_cast<int>(blockIdx.y);  // heaviest causal tiles first
+  const int qt = a.n_qtiles - 1 - static_cast<int>(blockIdx.x % a.n_qtiles);
   const int q0 = qt * BM;
   const int kv_tiles_all = (a.Sk + BN - 1) / BN;
   int n_kv = kv_tiles_all;
@@ -388,8 +390,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Ping-pong kernel: one CTA owns two adjacent 128-row query tiles X = 0 (rows [256t, +128))
 // and X = 1 (the next 128 rows) of one (b, h), sharing every K/V tile.
 //   warp 0        TMA producer (both Q tiles once, K_j and V_j through 2-slot rings)
-//   warp 1        TMEM allocation + UMMA issue
-//   warps 4-7     softmax for tile 0, warps 8-11 softmax for tile 1 (one query row each)
+//   warp 1        TMEM allocation + UMMA issue (warps 2-3 only hand their registers over)
+//   warps 4-7     softmax for tile 0, warps 8-11 softmax for tile 1 (one query row each; a
+//                 warp reads TMEM lanes 32*(warp % 4) .. +31, so each group covers 128 rows)
 // TMEM (512 columns): S_X at [128X, 128X+128), O_X at [256+128X, 256+128X+D). After the
 // softmax of tile X has read S_X(j) it overwrites S_X's first 64 columns with P_X(j) (fp16/
 // bf16 pairs), and O_X += P_X V_j is issued with A read from TMEM. Per tile the MMAs run
@@ -401,7 +404,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 // =======================================================================================
 constexpr int kPPThreads = 384;
 constexpr int kPPSoftmaxWarp0 = 4;
+// Register hand-off (setmaxnreg): warps 0-3 (TMA, UMMA, two spare) keep 56, the two softmax
+// warpgroups get 224; 56 * 128 + 224 * 256 = 168 * 384, the launch budget.
+constexpr int kPPRegsLaunch = 168;
+constexpr int kPPRegsLow = 56;
+constexpr int kPPRegsHigh = 224;
+static_assert(kPPRegsLow * 128 + kPPRegsHigh * 256 <= kPPRegsLaunch * kPPThreads,
+              "setmaxnreg split exceeds the launch register budget");
 constexpr float kLazyRescaleLog2 = 8.0f;
+
 
 template <int D>
 struct GeoPP {
@@ -444,11 +455,13 @@ __global__ void __launch_bounds__(kPPThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int bh = blockIdx.x;
+  // 1-D grid, head-major (a head's query-tile pairs are adjacent in launch order, so the
+  // resident CTAs share few heads' K/V in L2), heaviest causal pairs first.
+  const int n_pairs = (a.n_qtiles + 1) / 2;
+  const int bh = static_cast<int>(blockIdx.x / n_pairs);
   const int b = bh / a.H;
   const int h = bh % a.H;
-  const int n_pairs = (a.n_qtiles + 1) / 2;
-  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.y);  // heaviest causal pairs first
+  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.x % n_pairs);
   const int q0 = pair * 2 * BM;
   const int kv_tiles_all = (a.Sk + BN - 1) / BN;
   int nkv[2];
@@ -489,7 +502,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   const uint32_t sQ = smem_u32(smem + G::Q_OFF);
   const uint32_t sK = smem_u32(smem + G::K_OFF);
   const uint32_t sV = smem_u32(smem + G::V_OFF);
-
+  if (warp < kPPSoftmaxWarp0) {
+  regs_dec<kPPRegsLow>();
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
     if (lane == 0 && n_kv > 0) {
@@ -597,7 +611,9 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         if (next_k_ready) umma_commit(smem_u32(&k_empty[(j + 1) & 1]));
       }
     }
-  } else if (warp >= kPPSoftmaxWarp0) {
+  }
+  } else {
+    regs_inc<kPPRegsHigh>();
     // ------------------------------ softmax / epilogue ------------------------
     const int X = (warp - kPPSoftmaxWarp0) >> 2;
     const int quad = warp & 3;
@@ -620,54 +636,45 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       tc_fence_after();
       const int k0 = j * BN;
       const bool need_mask = (k0 + BN > a.Sk) || (a.causal && k0 + BN - 1 > qx0);
-      // Pass 1: row max of the scaled, masked scores.
-      float mx = -INFINITY;
+      // The whole S row in one TMEM round trip (four 32-column loads, one wait).
+      uint32_t sr[BN];
+      tmem_ld4x32(s_tm, sr);
+      if (need_mask) {
 #pragma unroll
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(s_tm + c, r);
-#pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          float v = __uint_as_float(r[t]) * a.scale_log2;
-          if (need_mask) {
-            const int kg = k0 + c + t;
-            if (kg >= a.Sk || (a.causal && kg > qg)) v = -INFINITY;
-          }
-          mx = fmaxf(mx, v);
+        for (int t = 0; t < BN; ++t) {
+          const int kg = k0 + t;
+          if (kg >= a.Sk || (a.causal && kg > qg)) sr[t] = __float_as_uint(-INFINITY);
         }
       }
+      // Row max on the raw scores (the scale is positive).
+      float mx = __uint_as_float(sr[0]);
+#pragma unroll
+      for (int t = 1; t < BN; ++t) mx = fmaxf(mx, __uint_as_float(sr[t]));
+      mx *= a.scale_log2;
       float alpha = 1.0f;
       bool rescale = false;
       if (m_use == -INFINITY) {
         m_use = mx;  // first tile: O not written yet, nothing to rescale
       } else if (mx > m_use + kLazyRescaleLog2) {
-        alpha = exp2f(m_use - mx);
+        alpha = ex2_approx(m_use - mx);
         m_use = mx;
         rescale = true;
       }
-      const float m_exp = m_use == -INFINITY ? 0.f : m_use;
-      // Pass 2: P = exp2(s - m) written over S's first 64 columns as packed pairs.
+      const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
+      // P = 2^(s * scale - m), packed in pairs over S's first 64 columns (S's values are all
+      // in registers by now).
       float psum = 0.f;
 #pragma unroll
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(s_tm + c, r);
-        uint32_t pk[16];
+      for (int hlf = 0; hlf < 2; ++hlf) {
+        uint32_t pk[32];
 #pragma unroll
-        for (int t = 0; t < 32; t += 2) {
-          float v0 = __uint_as_float(r[t]) * a.scale_log2;
-          float v1 = __uint_as_float(r[t + 1]) * a.scale_log2;
-          if (need_mask) {
-            const int kg = k0 + c + t;
-            if (kg >= a.Sk || (a.causal && kg > qg)) v0 = -INFINITY;
-            if (kg + 1 >= a.Sk || (a.causal && kg + 1 > qg)) v1 = -INFINITY;
-          }
-          const float p0 = exp2f(v0 - m_exp);
-          const float p1 = exp2f(v1 - m_exp);
+        for (int t = 0; t < 64; t += 2) {
+          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[64 * hlf + t]), a.scale_log2, neg_m));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[64 * hlf + t + 1]), a.scale_log2, neg_m));
           psum += p0 + p1;
           pk[t >> 1] = Pack2<T>::pack(p0, p1);
         }
-        tmem_st16(s_tm + (c >> 1), pk);
+        tmem_st32(s_tm + 32 * hlf, pk);
       }
       l_run = l_run * alpha + psum;
       // O_X is stable here: PV_X(j-1) was issued before QK_X(j), whose completion s_full
@@ -780,7 +787,7 @@ int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, in
     auto kern = flash_fwd_kernel<T, D>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(flash)");
-    dim3 grid(static_cast<unsigned>(B * H), static_cast<unsigned>(a.n_qtiles));
+    const unsigned grid = static_cast<unsigned>(B * H * a.n_qtiles);
     kern<<<grid, kThreads, G::SMEM_BYTES, st>>>(mq, mk, mv, a);
     return cuda_status(cudaGetLastError(), "flash launch");
   }
@@ -788,7 +795,19 @@ int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, in
   auto kern = flash_pp_kernel<T, D>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GP::SMEM_BYTES);
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(flash pp)");
-  dim3 grid(static_cast<unsigned>(B * H), static_cast<unsigned>((a.n_qtiles + 1) / 2));
+  // setmaxnreg.inc only completes if the launch holds the registers the split assumes.
+  cudaFuncAttributes fattr;
+  e = cudaFuncGetAttributes(&fattr, kern);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncGetAttributes(flash pp)");
+  if (fattr.numRegs != kPPRegsLaunch)
+    return fail(TLLM_ERR_CUDA, "flash_attention: kernel built with %d registers, %d expected",
+                fattr.numRegs, kPPRegsLaunch);
+  int resident = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kern, kPPThreads, GP::SMEM_BYTES);
+  if (e != cudaSuccess) return cuda_status(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor(flash pp)");
+  if (resident < 1)
+    return fail(TLLM_ERR_CUDA, "flash_attention: the two-tile kernel cannot be resident on this device");
+  const unsigned grid = static_cast<unsigned>(B * H * ((a.n_qtiles + 1) / 2));
   kern<<<grid, kPPThreads, GP::SMEM_BYTES, st>>>(mq, mk, mv, a);
   return cuda_status(cudaGetLastError(), "flash pp launch");
 }
@@ -829,7 +848,7 @@ int entry(const void *q, const void *k, const void *v, void *o, int64_t B, int64
   TLLM_CHECK_ARG(q && k && v && o, "flash_attention: null tensor pointer");
   TLLM_CHECK_ARG(Sq < (1LL << 31) && Sk < (1LL << 31) && B * H < (1LL << 31),
                  "flash_attention: problem too large");
-  TLLM_CHECK_ARG((Sq + 127) / 128 <= 65535, "flash_attention: Sq above 8388480 is not supported");
+  TLLM_CHECK_ARG(B * H * ((Sq + 127) / 128) < (1LL << 31), "flash_attention: grid too large");
   TLLM_CHECK_ARG(sq[3] == 1 && sk[3] == 1 && sv[3] == 1,
                  "flash_attention: q/k/v need a unit innermost stride");
   for (int i = 0; i < 3; ++i)

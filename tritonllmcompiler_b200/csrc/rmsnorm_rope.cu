@@ -41,6 +41,17 @@ __device__ __forceinline__ void load8(const T *p, float (&v)[8]) {
 }
 
 template <typename T>
+__device__ __forceinline__ void unpack8(const uint4 &raw, float (&v)[8]) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = Pack2<T>::unpack(w[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+template <typename T>
 __device__ __forceinline__ void store8(T *p, const float (&v)[8]) {
   uint4 raw;
   raw.x = Pack2<T>::pack(v[0], v[1]);
@@ -55,59 +66,70 @@ __device__ __forceinline__ float round_io(float v) {
   return to_f32<T>(from_f32<T>(v));
 }
 
-// Vector path: unit inner strides, 16-byte aligned rows. TPR = D / 16 threads per row.
-template <typename T, int D>
+// Vector path: unit inner strides, 16-byte aligned rows. TPR = D / 16 threads per row
+// group; each group handles R rows spaced G groups apart (G = groups in the grid), so a
+// warp's loads for one of its rows cover consecutive rows of memory, and the x vectors of
+// all R rows are requested before any is used (R * 32 bytes in flight per thread).
+template <typename T, int D, int R>
 __global__ void __launch_bounds__(256) rmsnorm_rope_vec_kernel(
     const T *__restrict__ x, const T *__restrict__ w, const T *__restrict__ cosb,
     const T *__restrict__ sinb, T *__restrict__ out, int64_t rows, RowGeom g, float eps) {
   constexpr int TPR = D / 16;
   constexpr int HALF = D / 2;
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t row = tid / TPR;
+  const int64_t group = tid / TPR;
+  const int64_t groups = static_cast<int64_t>(gridDim.x) * blockDim.x / TPR;
   const int part = static_cast<int>(tid % TPR);
-  // All TPR lanes of a row are in the same warp (TPR divides 32), so shuffles are safe even
-  // for the ragged last row group; lanes past the end compute on a clamped row and skip the
-  // store.
-  const bool valid = row < rows;
-  const int64_t r = valid ? row : rows - 1;
-  const int64_t h = r % g.H;
-  const int64_t bs = r / g.H;
-  const int64_t s = bs % g.S;
-  const int64_t b = bs / g.S;
-
-  const T *xr = x + b * g.sxb + s * g.sxs + h * g.sxh;
   const int c = part * 8;
-  float x1[8], x2[8], w1[8], w2[8];
-  load8<T>(xr + c, x1);
-  load8<T>(xr + HALF + c, x2);
+  // All TPR lanes of a group are in one warp (TPR divides 32), so the shuffles below are
+  // safe for every row slot; slots past the end compute on the last row and skip the store.
+  int64_t rr[R], ss[R], bb[R], hh[R];
+  uint4 x1r[R], x2r[R];
+#pragma unroll
+  for (int u = 0; u < R; ++u) {
+    const int64_t row = group + u * groups;
+    rr[u] = row;
+    const int64_t r = row < rows ? row : rows - 1;
+    hh[u] = r % g.H;
+    const int64_t bs = r / g.H;
+    ss[u] = bs % g.S;
+    bb[u] = bs / g.S;
+    const T *xr = x + bb[u] * g.sxb + ss[u] * g.sxs + hh[u] * g.sxh;
+    x1r[u] = __ldg(reinterpret_cast<const uint4 *>(xr + c));
+    x2r[u] = __ldg(reinterpret_cast<const uint4 *>(xr + HALF + c));
+  }
+  float w1[8], w2[8];
   load8<T>(w + c, w1);
   load8<T>(w + HALF + c, w2);
-
-  float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) ss = fmaf(x1[i], x1[i], fmaf(x2[i], x2[i], ss));
+  for (int u = 0; u < R; ++u) {
+    float x1[8], x2[8];
+    unpack8<T>(x1r[u], x1);
+    unpack8<T>(x2r[u], x2);
+    float ss2 = 0.f;
 #pragma unroll
-  for (int off = TPR / 2; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-  const float rstd = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), eps));
-
-  float c1[8], c2[8], s1[8], s2[8];
-  load8<T>(cosb + s * g.scs + c, c1);
-  load8<T>(cosb + s * g.scs + HALF + c, c2);
-  load8<T>(sinb + s * g.sss + c, s1);
-  load8<T>(sinb + s * g.sss + HALF + c, s2);
-
-  float o1[8], o2[8];
+    for (int i = 0; i < 8; ++i) ss2 = fmaf(x1[i], x1[i], fmaf(x2[i], x2[i], ss2));
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float y1 = round_io<T>(__fmul_rn(__fmul_rn(x1[i], rstd), w1[i]));
-    const float y2 = round_io<T>(__fmul_rn(__fmul_rn(x2[i], rstd), w2[i]));
-    o1[i] = __fsub_rn(__fmul_rn(y1, c1[i]), __fmul_rn(y2, s1[i]));
-    o2[i] = __fadd_rn(__fmul_rn(y2, c2[i]), __fmul_rn(y1, s2[i]));
-  }
-  if (valid) {
-    T *orow = out + b * g.sob + s * g.sos + h * g.soh;
-    store8<T>(orow + c, o1);
-    store8<T>(orow + HALF + c, o2);
+    for (int off = TPR / 2; off > 0; off >>= 1) ss2 += __shfl_xor_sync(0xffffffffu, ss2, off);
+    const float rstd = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss2, static_cast<float>(D)), eps));
+    float c1[8], c2[8], s1[8], s2[8];
+    load8<T>(cosb + ss[u] * g.scs + c, c1);
+    load8<T>(cosb + ss[u] * g.scs + HALF + c, c2);
+    load8<T>(sinb + ss[u] * g.sss + c, s1);
+    load8<T>(sinb + ss[u] * g.sss + HALF + c, s2);
+    float o1[8], o2[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float y1 = round_io<T>(__fmul_rn(__fmul_rn(x1[i], rstd), w1[i]));
+      const float y2 = round_io<T>(__fmul_rn(__fmul_rn(x2[i], rstd), w2[i]));
+      o1[i] = __fsub_rn(__fmul_rn(y1, c1[i]), __fmul_rn(y2, s1[i]));
+      o2[i] = __fadd_rn(__fmul_rn(y2, c2[i]), __fmul_rn(y1, s2[i]));
+    }
+    if (rr[u] < rows) {
+      T *orow = out + bb[u] * g.sob + ss[u] * g.sos + hh[u] * g.soh;
+      store8<T>(orow + c, o1);
+      store8<T>(orow + HALF + c, o2);
+    }
   }
 }
 
@@ -157,13 +179,26 @@ int launch(const void *x, const void *w, const void *c, const void *s, void *o, 
   const T *sp = static_cast<const T *>(s);
   T *op = static_cast<T *>(o);
   if (vec) {
-    const int64_t threads = rows * (D / 16);
+    // Rows per thread group: 4 once there is enough work to keep every SM busy.
+    constexpr int R = 4;
+    const int64_t tpr = D / 16;
+    const int64_t groups = rows >= 4 * 148 * 256 ? (rows + R - 1) / R : rows;
+    const int64_t threads = groups * tpr;
     const unsigned grid = static_cast<unsigned>((threads + 255) / 256);
-    switch (D) {
-      case 16: rmsnorm_rope_vec_kernel<T, 16><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
-      case 32: rmsnorm_rope_vec_kernel<T, 32><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
-      case 64: rmsnorm_rope_vec_kernel<T, 64><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
-      default: rmsnorm_rope_vec_kernel<T, 128><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
+    if (groups != rows) {
+      switch (D) {
+        case 16: rmsnorm_rope_vec_kernel<T, 16, R><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
+        case 32: rmsnorm_rope_vec_kernel<T, 32, R><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
+        case 64: rmsnorm_rope_vec_kernel<T, 64, R><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
+        default: rmsnorm_rope_vec_kernel<T, 128, R><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
+      }
+    } else {
+      switch (D) {
+        case 16: rmsnorm_rope_vec_kernel<T, 16, 1><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
+        case 32: rmsnorm_rope_vec_kernel<T, 32, 1><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
+        case 64: rmsnorm_rope_vec_kernel<T, 64, 1><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
+        default: rmsnorm_rope_vec_kernel<T, 128, 1><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
+      }
     }
   } else {
     const unsigned grid = static_cast<unsigned>((rows + 127) / 128);
