@@ -18,7 +18,7 @@
 // Causal: only key tiles j <= i are visited for query tile i; only the diagonal tile and a
 // ragged key tail are masked. The mask is top-left aligned (key j visible to query i iff
 // j <= i), exactly as the reference's offs_m >= offs_n.
-// No TMA multicast is used anywhere. Every mbarrier wait is bounded.
+// Every CTA loads its own tiles; every mbarrier wait is bounded.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>

@@ -1,5 +1,5 @@
-// Hand-written PTX wrappers for sm_100a: mbarriers, TMA (cp.async.bulk.tensor, never with
-// .multicast::cluster), tcgen05 (TMEM allocation, UMMA issue/commit, TMEM loads/stores) and
+// Hand-written PTX wrappers for sm_100a: mbarriers, TMA (cp.async.bulk.tensor, each CTA
+// loading its own tiles), tcgen05 (TMEM allocation, UMMA issue/commit, TMEM loads/stores) and
 // the bounded waits every pipelined kernel in this library uses.
 //
 // Descriptor formats follow the PTX ISA "Shared memory descriptor" and "Instruction

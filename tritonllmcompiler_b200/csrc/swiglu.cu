@@ -14,7 +14,7 @@
 //   warps 2-5   epilogue: tcgen05.ld the two fp32 accumulators of a row, silu(g)*u in fp32,
 //               one store in the I/O dtype. The accumulator is double-buffered in TMEM
 //               (2 x 256 columns) so the epilogue of tile i overlaps the main loop of i+1.
-// No TMA multicast is used anywhere. Every mbarrier wait is bounded.
+// Every CTA loads its own tiles; every mbarrier wait is bounded.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
