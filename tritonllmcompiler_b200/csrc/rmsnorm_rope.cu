@@ -66,41 +66,68 @@ __device__ __forceinline__ float round_io(float v) {
   return to_f32<T>(from_f32<T>(v));
 }
 
-// Vector path: unit inner strides, 16-byte aligned rows. TPR = D / 16 threads per row
-// group; each group handles R rows spaced G groups apart (G = groups in the grid), so a
-// warp's loads for one of its rows cover consecutive rows of memory, and the x vectors of
-// all R rows are requested before any is used (R * 32 bytes in flight per thread).
+// Streaming global accesses: x is read once (no L1 allocation), out is written once.
+__device__ __forceinline__ uint4 ld_stream(const void *p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ void st_stream(void *p, const uint4 &v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
+  uint4 raw;
+  raw.x = Pack2<T>::pack(v[0], v[1]);
+  raw.y = Pack2<T>::pack(v[2], v[3]);
+  raw.z = Pack2<T>::pack(v[4], v[5]);
+  raw.w = Pack2<T>::pack(v[6], v[7]);
+  return raw;
+}
+
+// Vector path: unit inner strides, 16-byte aligned rows. A group of TPR = D / 16 threads
+// handles R consecutive heads of one (b, s) position: each thread owns one 16-byte vector
+// of the first half of D and the matching vector of the second half, requests the x vectors
+// of all R rows up front (R * 32 bytes in flight per thread), and loads the weight and the
+// cos/sin vectors of position s once for the R rows. H % R == 0.
 template <typename T, int D, int R>
 __global__ void __launch_bounds__(256) rmsnorm_rope_vec_kernel(
     const T *__restrict__ x, const T *__restrict__ w, const T *__restrict__ cosb,
-    const T *__restrict__ sinb, T *__restrict__ out, int64_t rows, RowGeom g, float eps) {
+    const T *__restrict__ sinb, T *__restrict__ out, int64_t groups, RowGeom g, float eps) {
   constexpr int TPR = D / 16;
   constexpr int HALF = D / 2;
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t group = tid / TPR;
-  const int64_t groups = static_cast<int64_t>(gridDim.x) * blockDim.x / TPR;
-  const int part = static_cast<int>(tid % TPR);
-  const int c = part * 8;
-  // All TPR lanes of a group are in one warp (TPR divides 32), so the shuffles below are
-  // safe for every row slot; slots past the end compute on the last row and skip the store.
-  int64_t rr[R], ss[R], bb[R], hh[R];
+  const int64_t gi_raw = tid / TPR;
+  // All TPR lanes of a group sit in one warp (TPR divides 32), so the shuffles below are
+  // safe; a group past the end recomputes the last group and skips its stores.
+  const bool valid = gi_raw < groups;
+  const int64_t gi = valid ? gi_raw : groups - 1;
+  const int c = static_cast<int>(tid % TPR) * 8;
+  const int64_t row0 = gi * R;
+  const int64_t h0 = row0 % g.H;
+  const int64_t bs = row0 / g.H;
+  const int64_t s = bs % g.S;
+  const int64_t b = bs / g.S;
+  const T *xr = x + b * g.sxb + s * g.sxs + h0 * g.sxh;
   uint4 x1r[R], x2r[R];
 #pragma unroll
   for (int u = 0; u < R; ++u) {
-    const int64_t row = group + u * groups;
-    rr[u] = row;
-    const int64_t r = row < rows ? row : rows - 1;
-    hh[u] = r % g.H;
-    const int64_t bs = r / g.H;
-    ss[u] = bs % g.S;
-    bb[u] = bs / g.S;
-    const T *xr = x + bb[u] * g.sxb + ss[u] * g.sxs + hh[u] * g.sxh;
-    x1r[u] = __ldg(reinterpret_cast<const uint4 *>(xr + c));
-    x2r[u] = __ldg(reinterpret_cast<const uint4 *>(xr + HALF + c));
+    x1r[u] = ld_stream(xr + u * g.sxh + c);
+    x2r[u] = ld_stream(xr + u * g.sxh + HALF + c);
   }
-  float w1[8], w2[8];
+  float w1[8], w2[8], c1[8], c2[8], s1[8], s2[8];
   load8<T>(w + c, w1);
   load8<T>(w + HALF + c, w2);
+  load8<T>(cosb + s * g.scs + c, c1);
+  load8<T>(cosb + s * g.scs + HALF + c, c2);
+  load8<T>(sinb + s * g.sss + c, s1);
+  load8<T>(sinb + s * g.sss + HALF + c, s2);
+  T *orow = out + b * g.sob + s * g.sos + h0 * g.soh;
 #pragma unroll
   for (int u = 0; u < R; ++u) {
     float x1[8], x2[8];
@@ -112,11 +139,6 @@ __global__ void __launch_bounds__(256) rmsnorm_rope_vec_kernel(
 #pragma unroll
     for (int off = TPR / 2; off > 0; off >>= 1) ss2 += __shfl_xor_sync(0xffffffffu, ss2, off);
     const float rstd = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss2, static_cast<float>(D)), eps));
-    float c1[8], c2[8], s1[8], s2[8];
-    load8<T>(cosb + ss[u] * g.scs + c, c1);
-    load8<T>(cosb + ss[u] * g.scs + HALF + c, c2);
-    load8<T>(sinb + ss[u] * g.sss + c, s1);
-    load8<T>(sinb + ss[u] * g.sss + HALF + c, s2);
     float o1[8], o2[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -125,10 +147,9 @@ __global__ void __launch_bounds__(256) rmsnorm_rope_vec_kernel(
       o1[i] = __fsub_rn(__fmul_rn(y1, c1[i]), __fmul_rn(y2, s1[i]));
       o2[i] = __fadd_rn(__fmul_rn(y2, c2[i]), __fmul_rn(y1, s2[i]));
     }
-    if (rr[u] < rows) {
-      T *orow = out + bb[u] * g.sob + ss[u] * g.sos + hh[u] * g.soh;
-      store8<T>(orow + c, o1);
-      store8<T>(orow + HALF + c, o2);
+    if (valid) {
+      st_stream(orow + u * g.soh + c, pack8<T>(o1));
+      st_stream(orow + u * g.soh + HALF + c, pack8<T>(o2));
     }
   }
 }
@@ -179,27 +200,29 @@ int launch(const void *x, const void *w, const void *c, const void *s, void *o, 
   const T *sp = static_cast<const T *>(s);
   T *op = static_cast<T *>(o);
   if (vec) {
-    // Rows per thread group: 4 once there is enough work to keep every SM busy.
-    constexpr int R = 4;
-    const int64_t tpr = D / 16;
-    const int64_t groups = rows >= 4 * 148 * 256 ? (rows + R - 1) / R : rows;
-    const int64_t threads = groups * tpr;
+    // Heads per thread group: 4 when H allows it and there is work for every SM many times
+    // over, else 2 or 1.
+    const int64_t H = g.H;
+    int R = 1;
+    if (H % 4 == 0 && rows >= 4LL * 148 * 256) R = 4;
+    else if (H % 2 == 0 && rows >= 2LL * 148 * 256) R = 2;
+    const int64_t groups = rows / R;
+    const int64_t threads = groups * (D / 16);
     const unsigned grid = static_cast<unsigned>((threads + 255) / 256);
-    if (groups != rows) {
-      switch (D) {
-        case 16: rmsnorm_rope_vec_kernel<T, 16, R><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
-        case 32: rmsnorm_rope_vec_kernel<T, 32, R><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
-        case 64: rmsnorm_rope_vec_kernel<T, 64, R><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
-        default: rmsnorm_rope_vec_kernel<T, 128, R><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
-      }
-    } else {
-      switch (D) {
-        case 16: rmsnorm_rope_vec_kernel<T, 16, 1><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
-        case 32: rmsnorm_rope_vec_kernel<T, 32, 1><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
-        case 64: rmsnorm_rope_vec_kernel<T, 64, 1><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
-        default: rmsnorm_rope_vec_kernel<T, 128, 1><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, rows, g, eps); break;
-      }
+#define TLLM_RR_LAUNCH(DD, RR)                                                                \
+  rmsnorm_rope_vec_kernel<T, DD, RR><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, groups, g, eps)
+#define TLLM_RR_BY_R(DD)            \
+  if (R == 4) TLLM_RR_LAUNCH(DD, 4); \
+  else if (R == 2) TLLM_RR_LAUNCH(DD, 2); \
+  else TLLM_RR_LAUNCH(DD, 1);
+    switch (D) {
+      case 16: TLLM_RR_BY_R(16) break;
+      case 32: TLLM_RR_BY_R(32) break;
+      case 64: TLLM_RR_BY_R(64) break;
+      default: TLLM_RR_BY_R(128) break;
     }
+#undef TLLM_RR_BY_R
+#undef TLLM_RR_LAUNCH
   } else {
     const unsigned grid = static_cast<unsigned>((rows + 127) / 128);
     rmsnorm_rope_strided_kernel<T><<<grid, 128, 0, st>>>(xp, wp, cp, sp, op, rows,
