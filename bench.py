@@ -4,7 +4,8 @@
 Headline workload (N=1): swiglu at the Llama-3-8B MLP shape, x [4096, 4096], w1/w3
 [4096, 14336] fp16 (seed 1), metric TFLOP/s = 4*M*N*K / time. With N GPUs (torchrun, one
 process per GPU) the same problem is column-sharded over N (each rank computes
-out[:, N/g slice]) and the output is all-gathered over NVLink with NCCL (strong scaling).
+out[:, N/g slice]); the GEMM epilogue stores each tile into every rank's [M, N] output over
+NVLink (CUDA IPC peer buffers), or with --comm nccl the slices are all-gathered (strong scaling).
 At N=1 the line also carries the other three operators at their configurations under
 "ops" (rmsnorm_rope, flash_attention causal/non-causal, paged_attention decode).
 
@@ -45,7 +46,10 @@ def parse():
     ap.add_argument("--no-ops", action="store_true", help="skip the per-operator extras")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--chunks", type=int, default=1,
-                    help="N>1: row chunks whose all-gather overlaps the next chunk's GEMM")
+                    help="N>1 with --comm nccl: row chunks whose all-gather overlaps the next GEMM")
+    ap.add_argument("--comm", choices=["peers", "nccl"], default="peers",
+                    help="N>1: peers = the GEMM epilogue stores into every rank's output over "
+                         "NVLink; nccl = all_gather_into_tensor + permute")
     ap.add_argument("--op", choices=sorted(OP_CASES), default=None,
                     help="run only this operator case (steps+warmup launches) and print its timing")
     return ap.parse_args()
@@ -380,7 +384,6 @@ def run_ours(args):
     w1l = w1[:, rank * n_loc:(rank + 1) * n_loc].contiguous()
     w3l = w3[:, rank * n_loc:(rank + 1) * n_loc].contiguous()
     del w1, w3
-    gathered = torch.empty(world * M * n_loc, dtype=torch.float16, device="cuda") if world > 1 else None
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
 
     def kernel_only():
@@ -388,11 +391,19 @@ def run_ours(args):
 
     from tritonllmcompiler_b200 import sharded as S
 
-    out_full = torch.empty((M, N), dtype=torch.float16, device="cuda") if world > 1 else None
+    out_full = None
+    peers = None
+    if world > 1:
+        if args.comm == "peers":
+            peers = S.PeerBuffers((M, N), torch.float16, torch.device("cuda", local))
+        else:
+            out_full = torch.empty((M, N), dtype=torch.float16, device="cuda")
 
     def step():
         if world == 1:
             return T.swiglu(x, w1l, w3l)
+        if peers is not None:
+            return S.swiglu_column_sharded(x, w1l, w3l, peers=peers)
         return S.swiglu_column_sharded(x, w1l, w3l, chunks=args.chunks, out=out_full)
 
     flops = 4.0 * M * K * N
@@ -428,13 +439,19 @@ def run_ours(args):
     hout = torch.empty((M, n_loc), dtype=torch.float16).pin_memory()
     dx, d1, d3 = torch.empty_like(x), torch.empty_like(w1l), torch.empty_like(w3l)
 
+    if world > 1:
+        hout = torch.empty((M, N), dtype=torch.float16).pin_memory()
+
     def e2e_step():
         dx.copy_(hx, non_blocking=True)
         d1.copy_(h1, non_blocking=True)
         d3.copy_(h3, non_blocking=True)
-        out = T.swiglu(dx, d1, d3)
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, out)
+        if world == 1:
+            out = T.swiglu(dx, d1, d3)
+        elif peers is not None:
+            out = S.swiglu_column_sharded(dx, d1, d3, peers=peers)
+        else:
+            out = S.swiglu_column_sharded(dx, d1, d3, chunks=args.chunks, out=out_full)
         hout.copy_(out, non_blocking=True)
 
     et = _events_time(torch, e2e_step, max(3, args.steps // 4), 2)
@@ -465,9 +482,12 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic (seeded normal, x~N(0,1), w~N(0,1/K))",
             "config": {"workload": f"swiglu M{M} K{K} N{N} fp16 (Llama-3-8B MLP)",
-                       "parallelism": "single GPU" if world == 1 else
-                       f"column-shard N over {world} ranks + NCCL all_gather_into_tensor + "
-                       f"permute into [M, N] ({args.chunks} row chunk(s))",
+                       "parallelism": "single GPU" if world == 1 else (
+                           f"column-shard N over {world} ranks; GEMM epilogue stores every "
+                           f"tile into all ranks' [M, N] outputs over NVLink (CUDA IPC)"
+                           if args.comm == "peers" else
+                           f"column-shard N over {world} ranks + NCCL all_gather_into_tensor + "
+                           f"permute into [M, N] ({args.chunks} row chunk(s))"),
                        "l2": "256 MiB buffer written between timed steps; inputs 267 MB > L2"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
@@ -482,6 +502,10 @@ def run_ours(args):
             line["ops"] = ops
         print(json.dumps(line), flush=True)
     if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()
+        if peers is not None:
+            peers.close()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -165,6 +165,29 @@ TLLM_API int tllm_swiglu(const void *x, const void *w1, const void *w3, void *ou
                 int64_t N, int64_t K, int64_t lda, int64_t ldb1, int64_t ldb3,
                 int64_t ldo, int dtype, void *stream);
 
+/*
+ * Column-sharded SwiGLU for one node (no counterpart in the reference, which is single-GPU):
+ * computes silu(x @ w1) * (x @ w3) for this rank's column slices w1/w3 [K, N] (N = this
+ * rank's share of the columns) and writes the [M, N] result at column offset col_off of
+ * EVERY buffer in dsts[0..ndst) (row stride ldo): this rank's [M, N_total] output and the
+ * peers' outputs mapped into this process (tllm_ipc_open). The GEMM epilogue stores straight
+ * over NVLink, so the all-gather costs no separate pass. The caller orders the call after
+ * every peer has finished reading its previous output and before any rank reads the new one
+ * (for example a small NCCL all-reduce before and after). ndst <= 8; K, N, the leading
+ * dimensions and col_off multiples of 8.
+ */
+TLLM_API int tllm_swiglu_colshard(const void *x, const void *w1, const void *w3,
+                                  void *const *dsts, int ndst, int64_t col_off, int64_t M,
+                                  int64_t N, int64_t K, int64_t lda, int64_t ldb1, int64_t ldb3,
+                                  int64_t ldo, int dtype, void *stream);
+
+/* CUDA IPC set-up helpers for tllm_swiglu_colshard's peer buffers: a 64-byte handle and
+ * byte offset for a device pointer, opening a peer's handle in this process, and closing it.
+ * Not on the hot path. */
+TLLM_API int tllm_ipc_get_handle(const void *ptr, void *handle_out, uint64_t *offset_out);
+TLLM_API int tllm_ipc_open(const void *handle, uint64_t offset, void **ptr_out, void **base_out);
+TLLM_API int tllm_ipc_close(void *base);
+
 #ifdef __cplusplus
 }
 #endif

@@ -51,6 +51,15 @@ SIGNATURES = {
         [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _c_i64p, _i64, _c_i64p, _c_i64p,
          _c_i64p, ctypes.c_float, ctypes.c_int, _vp],
     ),
+    "tllm_swiglu_colshard": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, _i64, _i64, _i64, _i64,
+         _i64, _i64, _i64, _i64, ctypes.c_int, _vp],
+    ),
+    "tllm_ipc_get_handle": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(ctypes.c_uint64)]),
+    "tllm_ipc_open": (ctypes.c_int, [_vp, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p),
+                                     ctypes.POINTER(ctypes.c_void_p)]),
+    "tllm_ipc_close": (ctypes.c_int, [_vp]),
     "tllm_swiglu": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_int, _vp],

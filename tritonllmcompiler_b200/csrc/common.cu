@@ -121,4 +121,50 @@ int tllm_debug_status(int *out) {
   return tllm::read_and_clear_device_status(out);
 }
 
+// ---- CUDA IPC plumbing for peer output buffers (set-up, not the hot path) ----
+
+int tllm_ipc_get_handle(const void *ptr, void *handle_out, uint64_t *offset_out) {
+  tllm::clear_error();
+  if (!ptr || !handle_out || !offset_out)
+    return tllm::fail(TLLM_ERR_INVALID, "tllm_ipc_get_handle: null argument");
+  static PFN_cuMemGetAddressRange_v3020 range_fn = nullptr;
+  if (!range_fn) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+      return tllm::fail(TLLM_ERR_CUDA, "cuMemGetAddressRange is not available from the driver");
+    range_fn = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range_fn(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return tllm::fail(TLLM_ERR_INVALID, "tllm_ipc_get_handle: pointer is not device memory");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(base));
+  if (e != cudaSuccess) return tllm::cuda_status(e, "cudaIpcGetMemHandle");
+  memcpy(handle_out, &h, sizeof(h));
+  *offset_out = reinterpret_cast<uint64_t>(ptr) - static_cast<uint64_t>(base);
+  return TLLM_OK;
+}
+
+int tllm_ipc_open(const void *handle, uint64_t offset, void **ptr_out, void **base_out) {
+  tllm::clear_error();
+  if (!handle || !ptr_out || !base_out)
+    return tllm::fail(TLLM_ERR_INVALID, "tllm_ipc_open: null argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void *base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return tllm::cuda_status(e, "cudaIpcOpenMemHandle");
+  *base_out = base;
+  *ptr_out = static_cast<char *>(base) + offset;
+  return TLLM_OK;
+}
+
+int tllm_ipc_close(void *base) {
+  tllm::clear_error();
+  return tllm::cuda_status(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle");
+}
+
 }  // extern "C"

@@ -96,7 +96,7 @@ __device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
 // of all R rows up front (R * 32 bytes in flight per thread), and loads the weight and the
 // cos/sin vectors of position s once for the R rows. H % R == 0.
 template <typename T, int D, int R>
-__global__ void __launch_bounds__(256) rmsnorm_rope_vec_kernel(
+__global__ void __launch_bounds__(256, 2) rmsnorm_rope_vec_kernel(
     const T *__restrict__ x, const T *__restrict__ w, const T *__restrict__ cosb,
     const T *__restrict__ sinb, T *__restrict__ out, int64_t groups, RowGeom g, float eps) {
   constexpr int TPR = D / 16;
@@ -200,11 +200,12 @@ int launch(const void *x, const void *w, const void *c, const void *s, void *o, 
   const T *sp = static_cast<const T *>(s);
   T *op = static_cast<T *>(o);
   if (vec) {
-    // Heads per thread group: 4 when H allows it and there is work for every SM many times
-    // over, else 2 or 1.
+    // Heads per thread group: 8 (or 4, 2) when H allows it and there is work for every SM
+    // many times over; two 256-thread blocks stay resident per SM (register cap 128).
     const int64_t H = g.H;
     int R = 1;
-    if (H % 4 == 0 && rows >= 4LL * 148 * 256) R = 4;
+    if (H % 8 == 0 && rows >= 8LL * 148 * 256) R = 8;
+    else if (H % 4 == 0 && rows >= 4LL * 148 * 256) R = 4;
     else if (H % 2 == 0 && rows >= 2LL * 148 * 256) R = 2;
     const int64_t groups = rows / R;
     const int64_t threads = groups * (D / 16);
@@ -212,7 +213,8 @@ int launch(const void *x, const void *w, const void *c, const void *s, void *o, 
 #define TLLM_RR_LAUNCH(DD, RR)                                                                \
   rmsnorm_rope_vec_kernel<T, DD, RR><<<grid, 256, 0, st>>>(xp, wp, cp, sp, op, groups, g, eps)
 #define TLLM_RR_BY_R(DD)            \
-  if (R == 4) TLLM_RR_LAUNCH(DD, 4); \
+  if (R == 8) TLLM_RR_LAUNCH(DD, 8); \
+  else if (R == 4) TLLM_RR_LAUNCH(DD, 4); \
   else if (R == 2) TLLM_RR_LAUNCH(DD, 2); \
   else TLLM_RR_LAUNCH(DD, 1);
     switch (D) {

@@ -53,6 +53,11 @@ constexpr int TMEM_COLS = 512;                       // two accumulator buffers
 constexpr int kThreads = 192;
 constexpr int kEpiThreads = 128;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*barriers*/ + 1024 /*alignment*/;
+// Column-sharded mode: per epilogue thread, kPeerBufs rotating 64-byte staging slots that the
+// bulk copies to the destinations read from.
+constexpr int kPeerBufs = 4;
+constexpr int PEER_STAGE_BYTES = kPeerBufs * 128 * 64;
+constexpr int SMEM_BYTES_PEERS = SMEM_BYTES + PEER_STAGE_BYTES;
 
 enum : int {
   SITE_EMPTY = 1,
@@ -61,11 +66,19 @@ enum : int {
   SITE_TFULL = 4,
 };
 
+constexpr int kMaxDst = 8;
+
 struct Geom {
   int M, N, K;
   int tiles_m, tiles_n, k_blocks;
   int64_t ldo;
-  int vec_store;  // 16-byte stores allowed (ldo % 8 == 0 and out 16-byte aligned)
+  int vec_store;  // 16-byte stores allowed (ldo % 8 == 0 and every destination aligned)
+  // Column-sharded mode (ndst > 0): each output tile is written at column offset col_off
+  // of every destination (this rank's [M, N_total] buffer and its peers', over NVLink)
+  // instead of to `out`.
+  int ndst;
+  int64_t col_off;
+  void *dst[kMaxDst];
 };
 
 template <typename T>
@@ -88,7 +101,25 @@ __device__ __forceinline__ void store_row_chunk(T *orow, int n_base, int N, bool
   }
 }
 
-template <typename T>
+// Asynchronous bulk copy of `bytes` (a multiple of 16) from shared to global memory, tracked
+// in the issuing thread's bulk async-group.
+__device__ __forceinline__ void bulk_store(void *dst, uint32_t src_smem, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+               "r"(src_smem), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+template <typename T, bool kPeers>
 __global__ void __launch_bounds__(kThreads, 1)
     swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                      const __grid_constant__ CUtensorMap tm_w1,
@@ -219,6 +250,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------ epilogue ----------------------------------
     const int quad = warp & 3;  // TMEM lanes this warp may access
     const int row = quad * 32 + lane;
+    uint8_t *peer_stage = smem + SMEM_BYTES - 1024;  // past the barrier block (peer mode only)
+    int peer_buf = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -243,7 +276,38 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float uv = __uint_as_float(ur[j]);
           v[j] = (gv / (1.0f + expf(-gv))) * uv;
         }
-        if (m < g.M) store_row_chunk<T>(orow, n0 + c, g.N, g.vec_store != 0, v);
+        if (!kPeers) {
+          if (m < g.M) store_row_chunk<T>(orow, n0 + c, g.N, g.vec_store != 0, v);
+        } else if (m < g.M) {
+          if (g.vec_store && n0 + c + 32 <= g.N) {
+            // Stage the 64-byte chunk, then one bulk copy per destination; the slot is reused
+            // kPeerBufs chunks later, once its copies have read it.
+            bulk_wait_read<kPeerBufs - 1>();
+            uint8_t *slot = peer_stage + (peer_buf * 128 + row) * 64;
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              uint4 raw;
+              raw.x = Pack2<T>::pack(v[j + 0], v[j + 1]);
+              raw.y = Pack2<T>::pack(v[j + 2], v[j + 3]);
+              raw.z = Pack2<T>::pack(v[j + 4], v[j + 5]);
+              raw.w = Pack2<T>::pack(v[j + 6], v[j + 7]);
+              *reinterpret_cast<uint4 *>(slot + j * 2) = raw;
+            }
+            fence_proxy_async_smem();
+            const int64_t off = static_cast<int64_t>(m) * g.ldo + g.col_off + n0 + c;
+#pragma unroll 1
+            for (int d = 0; d < g.ndst; ++d)
+              bulk_store(static_cast<T *>(g.dst[d]) + off, smem_u32(slot), 64);
+            bulk_commit();
+            peer_buf = peer_buf + 1 == kPeerBufs ? 0 : peer_buf + 1;
+          } else {
+#pragma unroll 1
+            for (int d = 0; d < g.ndst; ++d) {
+              T *drow = static_cast<T *>(g.dst[d]) + static_cast<int64_t>(m) * g.ldo + g.col_off;
+              store_row_chunk<T>(drow, n0 + c, g.N, false, v);
+            }
+          }
+        }
       }
       tc_fence_before();
       mbar_arrive(smem_u32(&tempty[acc]));
@@ -252,6 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc_phase ^= 1;
       }
     }
+    if (kPeers) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -299,9 +364,14 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 template <typename T>
 int launch(const void *x, const void *w1, const void *w3, void *out, int64_t M, int64_t N,
-           int64_t K, int64_t lda, int64_t ldb1, int64_t ldb3, int64_t ldo, cudaStream_t st) {
+           int64_t K, int64_t lda, int64_t ldb1, int64_t ldb3, int64_t ldo, cudaStream_t st,
+           void *const *dsts = nullptr, int ndst = 0, int64_t col_off = 0) {
   const bool tma_ok = lda % 8 == 0 && ldb1 % 8 == 0 && ldb3 % 8 == 0 && aligned16(x) &&
                       aligned16(w1) && aligned16(w3) && K % 8 == 0 && N % 8 == 0;
+  if (!tma_ok && ndst > 0)
+    return fail(TLLM_ERR_INVALID,
+                "swiglu column-sharded: K, N and the leading dimensions must be multiples of 8 "
+                "and x, w1, w3 16-byte aligned");
   if (!tma_ok) {
     dim3 grid(static_cast<unsigned>((N + 15) / 16), static_cast<unsigned>((M + 15) / 16));
     swiglu_simt_kernel<T><<<grid, 256, 0, st>>>(
@@ -341,15 +411,31 @@ int launch(const void *x, const void *w1, const void *w3, void *out, int64_t M, 
   g.tiles_n = static_cast<int>((N + BN - 1) / BN);
   g.k_blocks = static_cast<int>((K + BK - 1) / BK);
   g.ldo = ldo;
-  g.vec_store = (ldo % 8 == 0 && aligned16(out)) ? 1 : 0;
-  auto kern = swiglu_tc_kernel<T>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(swiglu)");
+  g.ndst = ndst;
+  g.col_off = col_off;
+  bool dst_aligned = true;
+  for (int d = 0; d < kMaxDst; ++d) {
+    g.dst[d] = d < ndst ? dsts[d] : nullptr;
+    if (d < ndst) dst_aligned = dst_aligned && aligned16(dsts[d]);
+  }
+  g.vec_store = (ldo % 8 == 0 && col_off % 8 == 0 && dst_aligned &&
+                 (ndst > 0 || aligned16(out))) ? 1 : 0;
   const int num_tiles = g.tiles_m * g.tiles_n;
   const int sms = sm_count();
   const int grid = num_tiles < sms ? num_tiles : sms;
-  kern<<<grid, kThreads, SMEM_BYTES, st>>>(mx, m1, m3, static_cast<T *>(out), g);
-  return cuda_status(cudaGetLastError(), "swiglu launch");
+  if (ndst == 0) {
+    auto kern = swiglu_tc_kernel<T, false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(swiglu)");
+    kern<<<grid, kThreads, SMEM_BYTES, st>>>(mx, m1, m3, static_cast<T *>(out), g);
+    return cuda_status(cudaGetLastError(), "swiglu launch");
+  }
+  auto kern = swiglu_tc_kernel<T, true>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES_PEERS);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(swiglu peers)");
+  kern<<<grid, kThreads, SMEM_BYTES_PEERS, st>>>(mx, m1, m3, static_cast<T *>(out), g);
+  return cuda_status(cudaGetLastError(), "swiglu peers launch");
 }
 
 }  // namespace
@@ -380,4 +466,31 @@ extern "C" int tllm_swiglu(const void *x, const void *w1, const void *w3, void *
   if (dtype == TLLM_DTYPE_F16)
     return swiglu::launch<__half>(x, w1, w3, out, M, N, K, lda, ldb1, ldb3, ldo, st);
   return swiglu::launch<__nv_bfloat16>(x, w1, w3, out, M, N, K, lda, ldb1, ldb3, ldo, st);
+}
+
+extern "C" int tllm_swiglu_colshard(const void *x, const void *w1, const void *w3,
+                                    void *const *dsts, int ndst, int64_t col_off, int64_t M,
+                                    int64_t N, int64_t K, int64_t lda, int64_t ldb1, int64_t ldb3,
+                                    int64_t ldo, int dtype, void *stream) {
+  using namespace tllm;
+  clear_error();
+  TLLM_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "swiglu column-sharded: negative dimension");
+  TLLM_CHECK_ARG(dtype == TLLM_DTYPE_F16 || dtype == TLLM_DTYPE_BF16,
+                 "swiglu column-sharded: unsupported dtype %d", dtype);
+  TLLM_CHECK_ARG(dsts && ndst >= 1 && ndst <= swiglu::kMaxDst,
+                 "swiglu column-sharded: 1..%d destinations required", swiglu::kMaxDst);
+  TLLM_CHECK_ARG(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31),
+                 "swiglu column-sharded: dimension too large");
+  TLLM_CHECK_ARG(col_off >= 0 && ldo >= col_off + N, "swiglu column-sharded: columns outside the row");
+  if (M == 0 || N == 0) return TLLM_OK;
+  for (int d = 0; d < ndst; ++d)
+    TLLM_CHECK_ARG(dsts[d], "swiglu column-sharded: null destination %d", d);
+  TLLM_CHECK_ARG(K > 0 && x && w1 && w3, "swiglu column-sharded: K must be positive");
+  TLLM_CHECK_ARG(lda >= K && ldb1 >= N && ldb3 >= N, "swiglu column-sharded: leading dimension too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == TLLM_DTYPE_F16)
+    return swiglu::launch<__half>(x, w1, w3, dsts[0], M, N, K, lda, ldb1, ldb3, ldo, st, dsts,
+                                  ndst, col_off);
+  return swiglu::launch<__nv_bfloat16>(x, w1, w3, dsts[0], M, N, K, lda, ldb1, ldb3, ldo, st,
+                                       dsts, ndst, col_off);
 }

@@ -8,16 +8,19 @@ The reference is single-GPU only. Across the GPUs of one node the operators shar
   only their physical blocks, re-indexed into a rank-local pool; no communication
   (``partition_sequences``, ``localize_blocks``). Sequences are balanced by token count
   (greedy longest-first) because context lengths vary widely.
-* swiglu over output columns: rank r holds x and the column slices w1[:, Nr], w3[:, Nr],
-  computes out[:, Nr], and the slices are all-gathered over NVLink with NCCL
-  (``swiglu_column_sharded``). Row chunks let the gather of chunk c overlap the GEMM of
-  chunk c+1 on a second stream.
+* swiglu over output columns: rank r holds x and the column slices w1[:, Nr], w3[:, Nr] and
+  computes out[:, Nr] (``swiglu_column_sharded``). With ``PeerBuffers`` (the default in the
+  benchmark) the GEMM epilogue stores each output tile straight into every rank's [M, N]
+  buffer over NVLink, so there is no separate all-gather pass; without them the slices are
+  all-gathered with NCCL and permuted into [M, N] (row chunks let the gather of chunk c
+  overlap the GEMM of chunk c+1).
 
 The per-rank compute function is a parameter only so the partitioning and gather logic can
 be exercised on CPU ranks (gloo); the default is the CUDA operator.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Callable, Sequence
 
 import torch
@@ -106,15 +109,85 @@ def column_range(n: int, rank: int, world: int, align: int = 8) -> tuple[int, in
     return rank * per, (rank + 1) * per
 
 
+class PeerBuffers:
+    """One [rows, cols] buffer per rank, each mapped into every rank's process (CUDA IPC).
+
+    ``ptrs[r]`` is rank r's buffer as seen from this process; ``local`` is this rank's own
+    tensor. Create once per output shape (opening IPC handles is slow) and ``close()`` before
+    the process group goes away.
+    """
+
+    def __init__(self, shape, dtype, device, group=None):
+        from tritonllmcompiler_b200 import _lib
+
+        lib = _lib.load()
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.local = torch.empty(shape, dtype=dtype, device=device)
+        handle = (ctypes.c_char * 64)()
+        offset = ctypes.c_uint64(0)
+        with torch.cuda.device(device):
+            _lib.check(lib.tllm_ipc_get_handle(self.local.data_ptr(), handle, ctypes.byref(offset)))
+        infos = [None] * self.world
+        dist.all_gather_object(infos, (bytes(handle), offset.value), group=group)
+        self.ptrs: list[int] = []
+        self._bases: list[int] = []
+        with torch.cuda.device(device):
+            for r, (hb, off) in enumerate(infos):
+                if r == self.rank:
+                    self.ptrs.append(self.local.data_ptr())
+                    continue
+                ptr, base = ctypes.c_void_p(), ctypes.c_void_p()
+                _lib.check(lib.tllm_ipc_open(hb, off, ctypes.byref(ptr), ctypes.byref(base)))
+                self.ptrs.append(ptr.value)
+                self._bases.append(base.value)
+        self._arr = (ctypes.c_void_p * self.world)(*self.ptrs)
+        self._flag = torch.zeros(1, dtype=torch.float32, device=device)
+
+    def close(self):
+        from tritonllmcompiler_b200 import _lib
+
+        lib = _lib.load()
+        with torch.cuda.device(self.local.device):
+            for b in self._bases:
+                lib.tllm_ipc_close(b)
+        self._bases = []
+
+
+def _swiglu_into_peers(x, w1_local, w3_local, peers: PeerBuffers, group):
+    from tritonllmcompiler_b200 import _lib
+
+    m, k = x.shape
+    n_loc = w1_local.shape[1]
+    out = peers.local
+    assert out.shape == (m, n_loc * peers.world) and out.dtype == x.dtype
+    assert x.stride(1) == 1 and w1_local.stride(1) == 1 and w3_local.stride(1) == 1
+    # Every rank has finished with its previous output before any peer writes into it.
+    dist.all_reduce(peers._flag, group=group)
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.load().tllm_swiglu_colshard(
+            x.data_ptr(), w1_local.data_ptr(), w3_local.data_ptr(), peers._arr, peers.world,
+            peers.rank * n_loc, m, n_loc, k, x.stride(0), w1_local.stride(0), w3_local.stride(0),
+            out.stride(0), _lib.DTYPE_CODES[x.dtype], _lib.stream_of(x)))
+    # Every peer's tiles have landed in this rank's buffer.
+    dist.all_reduce(peers._flag, group=group)
+    return out
+
+
 def swiglu_column_sharded(x: torch.Tensor, w1_local: torch.Tensor, w3_local: torch.Tensor,
                           group=None, *, chunks: int = 1, op: Callable | None = None,
-                          out: torch.Tensor | None = None) -> torch.Tensor:
+                          out: torch.Tensor | None = None,
+                          peers: PeerBuffers | None = None) -> torch.Tensor:
     """out = silu(x @ w1) * (x @ w3) with w1/w3 column-sharded over the process group.
 
     Every rank passes the full x [M, K] and its column slices [K, N/g]; every rank returns
-    the full [M, N] output. With chunks > 1 the rows are processed in `chunks` blocks and
-    the all-gather of block c runs on a side stream (CUDA) while block c+1 computes.
+    the full [M, N] output. With ``peers`` (CUDA, one node) the kernel writes every rank's
+    output directly and ``peers.local`` is returned. Otherwise the slices are all-gathered;
+    with chunks > 1 the rows are processed in `chunks` blocks and the all-gather of block c
+    runs on a side stream (CUDA) while block c+1 computes.
     """
+    if peers is not None:
+        return _swiglu_into_peers(x, w1_local, w3_local, peers, group)
     if op is None:
         from tritonllmcompiler_b200.ops.swiglu import swiglu as op
     world = dist.get_world_size(group)
