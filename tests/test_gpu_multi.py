@@ -42,11 +42,13 @@ def _worker(rank, world, port, mode, q):
         n0, n1 = S.column_range(n, rank, world)
         w1l, w3l = w1[:, n0:n1].contiguous(), w3[:, n0:n1].contiguous()
         full = T.swiglu(x, w1, w3)
-        if mode == "peers":
-            peers = S.PeerBuffers((m, n), x.dtype, x.device)
+        if mode.startswith("peers"):
+            peers = S.PeerBuffers((m, n), x.dtype, x.device, slots=int(mode[-1]))
             ok = True
-            for _ in range(2):  # the buffers are reused across calls
+            for _ in range(3):  # the slots are reused across calls
                 peers.local.fill_(float("nan"))
+                torch.cuda.synchronize()
+                dist.barrier()
                 out = S.swiglu_column_sharded(x, w1l, w3l, peers=peers)
                 torch.cuda.synchronize()
                 ok = ok and bool(torch.equal(out, full))
@@ -61,7 +63,7 @@ def _worker(rank, world, port, mode, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["1", "2", "peers"])
+@pytest.mark.parametrize("mode", ["1", "2", "peers1", "peers2"])
 def test_swiglu_column_sharded_two_gpus(cuda_device, mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")

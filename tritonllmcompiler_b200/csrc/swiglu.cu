@@ -53,10 +53,9 @@ constexpr int TMEM_COLS = 512;                       // two accumulator buffers
 constexpr int kThreads = 192;
 constexpr int kEpiThreads = 128;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*barriers*/ + 1024 /*alignment*/;
-// Column-sharded mode: per epilogue thread, kPeerBufs rotating 64-byte staging slots that the
-// bulk copies to the destinations read from.
-constexpr int kPeerBufs = 4;
-constexpr int PEER_STAGE_BYTES = kPeerBufs * 128 * 64;
+// Column-sharded mode: per epilogue thread, one 256-byte staging slot holding its row of the
+// current output tile, which the bulk copies to the destinations read from.
+constexpr int PEER_STAGE_BYTES = 128 * BN * 2;
 constexpr int SMEM_BYTES_PEERS = SMEM_BYTES + PEER_STAGE_BYTES;
 
 enum : int {
@@ -251,7 +250,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad = warp & 3;  // TMEM lanes this warp may access
     const int row = quad * 32 + lane;
     uint8_t *peer_stage = smem + SMEM_BYTES - 1024;  // past the barrier block (peer mode only)
-    int peer_buf = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -264,6 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * ACC_COLS;
       const int m = m0 + row;
       T *orow = out + static_cast<int64_t>(m) * g.ldo;
+      int staged = 0;  // peer mode: 32-column chunks of this row staged for the bulk copies
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t gr[32], ur[32];
@@ -280,10 +279,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (m < g.M) store_row_chunk<T>(orow, n0 + c, g.N, g.vec_store != 0, v);
         } else if (m < g.M) {
           if (g.vec_store && n0 + c + 32 <= g.N) {
-            // Stage the 64-byte chunk, then one bulk copy per destination; the slot is reused
-            // kPeerBufs chunks later, once its copies have read it.
-            bulk_wait_read<kPeerBufs - 1>();
-            uint8_t *slot = peer_stage + (peer_buf * 128 + row) * 64;
+            // Stage the 64-byte chunk in this thread's row slot; the whole row goes out in one
+            // bulk copy per destination after the last chunk.
+            if (c == 0) bulk_wait_read<0>();  // the previous tile's copies have read the slot
+            uint8_t *slot = peer_stage + row * (BN * 2) + c * 2;
 #pragma unroll
             for (int j = 0; j < 32; j += 8) {
               uint4 raw;
@@ -293,13 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               raw.w = Pack2<T>::pack(v[j + 6], v[j + 7]);
               *reinterpret_cast<uint4 *>(slot + j * 2) = raw;
             }
-            fence_proxy_async_smem();
-            const int64_t off = static_cast<int64_t>(m) * g.ldo + g.col_off + n0 + c;
-#pragma unroll 1
-            for (int d = 0; d < g.ndst; ++d)
-              bulk_store(static_cast<T *>(g.dst[d]) + off, smem_u32(slot), 64);
-            bulk_commit();
-            peer_buf = peer_buf + 1 == kPeerBufs ? 0 : peer_buf + 1;
+            ++staged;
           } else {
 #pragma unroll 1
             for (int d = 0; d < g.ndst; ++d) {
@@ -308,6 +301,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+      }
+      if (kPeers && staged > 0) {
+        // Staged chunks are the leading ones of the row (only the N tail is stored directly).
+        fence_proxy_async_smem();
+        const uint32_t src = smem_u32(peer_stage + row * (BN * 2));
+        const int64_t off = static_cast<int64_t>(m) * g.ldo + g.col_off + n0;
+#pragma unroll 1
+        for (int d = 0; d < g.ndst; ++d)
+          bulk_store(static_cast<T *>(g.dst[d]) + off, src, staged * 64);
+        bulk_commit();
       }
       tc_fence_before();
       mbar_arrive(smem_u32(&tempty[acc]));

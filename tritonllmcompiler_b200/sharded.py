@@ -110,45 +110,61 @@ def column_range(n: int, rank: int, world: int, align: int = 8) -> tuple[int, in
 
 
 class PeerBuffers:
-    """One [rows, cols] buffer per rank, each mapped into every rank's process (CUDA IPC).
+    """[rows, cols] output buffers on every rank, each mapped into every rank's process
+    (CUDA IPC), used in ``slots`` alternating copies.
 
-    ``ptrs[r]`` is rank r's buffer as seen from this process; ``local`` is this rank's own
-    tensor. Create once per output shape (opening IPC handles is slow) and ``close()`` before
-    the process group goes away.
+    ``ptrs[slot][r]`` is rank r's buffer of that slot as seen from this process;
+    ``locals[slot]`` is this rank's own tensor. With two slots a call's output stays valid
+    until the call after next, as long as whatever reads it is ordered on the same stream
+    before that call; with one slot each call also waits for every rank to be done with the
+    previous output. Create once per output shape (opening IPC handles is slow) and
+    ``close()`` before the process group goes away.
     """
 
-    def __init__(self, shape, dtype, device, group=None):
+    def __init__(self, shape, dtype, device, group=None, slots: int = 2):
         from tritonllmcompiler_b200 import _lib
 
+        assert slots in (1, 2)
         lib = _lib.load()
+        self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
-        self.local = torch.empty(shape, dtype=dtype, device=device)
-        handle = (ctypes.c_char * 64)()
-        offset = ctypes.c_uint64(0)
-        with torch.cuda.device(device):
-            _lib.check(lib.tllm_ipc_get_handle(self.local.data_ptr(), handle, ctypes.byref(offset)))
-        infos = [None] * self.world
-        dist.all_gather_object(infos, (bytes(handle), offset.value), group=group)
-        self.ptrs: list[int] = []
+        self.slots = slots
+        self.calls = 0
+        self.locals = [torch.empty(shape, dtype=dtype, device=device) for _ in range(slots)]
+        self.ptrs: list[list[int]] = []
         self._bases: list[int] = []
-        with torch.cuda.device(device):
-            for r, (hb, off) in enumerate(infos):
-                if r == self.rank:
-                    self.ptrs.append(self.local.data_ptr())
-                    continue
-                ptr, base = ctypes.c_void_p(), ctypes.c_void_p()
-                _lib.check(lib.tllm_ipc_open(hb, off, ctypes.byref(ptr), ctypes.byref(base)))
-                self.ptrs.append(ptr.value)
-                self._bases.append(base.value)
-        self._arr = (ctypes.c_void_p * self.world)(*self.ptrs)
+        for t in self.locals:
+            handle = (ctypes.c_char * 64)()
+            offset = ctypes.c_uint64(0)
+            with torch.cuda.device(device):
+                _lib.check(lib.tllm_ipc_get_handle(t.data_ptr(), handle, ctypes.byref(offset)))
+            infos = [None] * self.world
+            dist.all_gather_object(infos, (bytes(handle), offset.value), group=group)
+            ptrs = []
+            with torch.cuda.device(device):
+                for r, (hb, off) in enumerate(infos):
+                    if r == self.rank:
+                        ptrs.append(t.data_ptr())
+                        continue
+                    ptr, base = ctypes.c_void_p(), ctypes.c_void_p()
+                    _lib.check(lib.tllm_ipc_open(hb, off, ctypes.byref(ptr), ctypes.byref(base)))
+                    ptrs.append(ptr.value)
+                    self._bases.append(base.value)
+            self.ptrs.append(ptrs)
+        self._arrs = [(ctypes.c_void_p * self.world)(*p) for p in self.ptrs]
         self._flag = torch.zeros(1, dtype=torch.float32, device=device)
+
+    @property
+    def local(self) -> torch.Tensor:
+        """This rank's buffer of the slot the next call writes."""
+        return self.locals[self.calls % self.slots]
 
     def close(self):
         from tritonllmcompiler_b200 import _lib
 
         lib = _lib.load()
-        with torch.cuda.device(self.local.device):
+        with torch.cuda.device(self.locals[0].device):
             for b in self._bases:
                 lib.tllm_ipc_close(b)
         self._bases = []
@@ -159,18 +175,21 @@ def _swiglu_into_peers(x, w1_local, w3_local, peers: PeerBuffers, group):
 
     m, k = x.shape
     n_loc = w1_local.shape[1]
-    out = peers.local
+    slot = peers.calls % peers.slots
+    out = peers.locals[slot]
     assert out.shape == (m, n_loc * peers.world) and out.dtype == x.dtype
     assert x.stride(1) == 1 and w1_local.stride(1) == 1 and w3_local.stride(1) == 1
-    # Every rank has finished with its previous output before any peer writes into it.
-    dist.all_reduce(peers._flag, group=group)
+    if peers.slots == 1:
+        # Every rank has finished with its previous output before any peer writes into it.
+        dist.all_reduce(peers._flag, group=group)
     with torch.cuda.device(x.device):
         _lib.check(_lib.load().tllm_swiglu_colshard(
-            x.data_ptr(), w1_local.data_ptr(), w3_local.data_ptr(), peers._arr, peers.world,
+            x.data_ptr(), w1_local.data_ptr(), w3_local.data_ptr(), peers._arrs[slot], peers.world,
             peers.rank * n_loc, m, n_loc, k, x.stride(0), w1_local.stride(0), w3_local.stride(0),
             out.stride(0), _lib.DTYPE_CODES[x.dtype], _lib.stream_of(x)))
     # Every peer's tiles have landed in this rank's buffer.
     dist.all_reduce(peers._flag, group=group)
+    peers.calls += 1
     return out
 
 
@@ -182,7 +201,7 @@ def swiglu_column_sharded(x: torch.Tensor, w1_local: torch.Tensor, w3_local: tor
 
     Every rank passes the full x [M, K] and its column slices [K, N/g]; every rank returns
     the full [M, N] output. With ``peers`` (CUDA, one node) the kernel writes every rank's
-    output directly and ``peers.local`` is returned. Otherwise the slices are all-gathered;
+    output directly and this rank's buffer of the slot just written is returned. Otherwise the slices are all-gathered;
     with chunks > 1 the rows are processed in `chunks` blocks and the all-gather of block c
     runs on a side stream (CUDA) while block c+1 computes.
     """
