@@ -646,10 +646,15 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           if (kg >= a.Sk || (a.causal && kg > qg)) sr[t] = __float_as_uint(-INFINITY);
         }
       }
-      // Row max on the raw scores (the scale is positive).
-      float mx = __uint_as_float(sr[0]);
+      // Row max on the raw scores (the scale is positive): an 8-way tree of 3-input maxima.
+      float mx8[8];
 #pragma unroll
-      for (int t = 1; t < BN; ++t) mx = fmaxf(mx, __uint_as_float(sr[t]));
+      for (int t = 0; t < 8; ++t) mx8[t] = __uint_as_float(sr[t]);
+#pragma unroll
+      for (int t = 8; t < BN; t += 2)
+        mx8[(t >> 1) & 7] = max3f(mx8[(t >> 1) & 7], __uint_as_float(sr[t]), __uint_as_float(sr[t + 1]));
+      float mx = max3f(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], mx8[5]),
+                       fmaxf(mx8[6], mx8[7]));
       mx *= a.scale_log2;
       float alpha = 1.0f;
       bool rescale = false;
@@ -663,19 +668,32 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
       // P = 2^(s * scale - m), packed in pairs over S's first 64 columns (S's values are all
       // in registers by now).
-      float psum = 0.f;
+      // Exponent arguments and the row sum use packed fp32 pairs (one instruction per pair).
+      const uint64_t scale2 = f2_pack(a.scale_log2, a.scale_log2);
+      const uint64_t negm2 = f2_pack(neg_m, neg_m);
+      uint64_t ps2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
       for (int hlf = 0; hlf < 2; ++hlf) {
         uint32_t pk[32];
 #pragma unroll
         for (int t = 0; t < 64; t += 2) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[64 * hlf + t]), a.scale_log2, neg_m));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[64 * hlf + t + 1]), a.scale_log2, neg_m));
-          psum += p0 + p1;
+          const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sr[64 * hlf + t]), __uint_as_float(sr[64 * hlf + t + 1])),
+                                     scale2, negm2);
+          float x0, x1;
+          f2_unpack(x2, x0, x1);
+          const float p0 = ex2_approx(x0);
+          const float p1 = ex2_approx(x1);
+          ps2[(t >> 1) & 3] = f2_add(ps2[(t >> 1) & 3], f2_pack(p0, p1));
           pk[t >> 1] = Pack2<T>::pack(p0, p1);
         }
         tmem_st32(s_tm + 32 * hlf, pk);
       }
+      float psa, psb, psc, psd, pse, psf, psg, psh;
+      f2_unpack(ps2[0], psa, psb);
+      f2_unpack(ps2[1], psc, psd);
+      f2_unpack(ps2[2], pse, psf);
+      f2_unpack(ps2[3], psg, psh);
+      const float psum = ((psa + psb) + (psc + psd)) + ((pse + psf) + (psg + psh));
       l_run = l_run * alpha + psum;
       // O_X is stable here: PV_X(j-1) was issued before QK_X(j), whose completion s_full
       // signalled.
