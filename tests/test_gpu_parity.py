@@ -252,7 +252,8 @@ def test_paged_int64_metadata_and_strided_q(cuda_device):
 
 
 @pytest.mark.parametrize("b,h,s,d,causal", [(2, 4, 1000, 128, True), (1, 4, 384, 64, False),
-                                            (1, 2, 300, 32, True), (1, 2, 257, 16, False)])
+                                            (1, 2, 300, 32, True), (1, 2, 257, 16, False),
+                                            (4, 64, 2048, 128, True), (2, 32, 1536, 64, False)])
 def test_flash_kernel_variants_agree(cuda_device, b, h, s, d, causal):
     """The two-tile ping-pong kernel (default) and the single-tile kernel agree."""
     from tritonllmcompiler_b200 import _lib
@@ -267,4 +268,5 @@ def test_flash_kernel_variants_agree(cuda_device, b, h, s, d, causal):
             _lib.strides(q), _lib.strides(k), _lib.strides(v), _lib.strides(o),
             d ** -0.5, int(causal), 0, variant, torch.cuda.current_stream().cuda_stream))
         outs.append(o)
-    assert torch.allclose(outs[0].float(), outs[1].float(), **G.tol(torch.float16))
+    for o in outs[1:]:
+        assert torch.allclose(outs[0].float(), o.float(), **G.tol(torch.float16))
