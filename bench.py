@@ -22,9 +22,7 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import threading
 import time
 from datetime import timedelta
@@ -78,60 +76,69 @@ def profile_traffic(name: str):
 
 
 class ClockSampler:
-    """Samples SM clocks and throttle reasons with nvidia-smi while the timed region runs."""
+    """Samples the SM clock and clock-event (throttle) reasons while the timed region runs.
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NVML is read from a background thread every millisecond (a timed region of a few tens
+    of milliseconds would fall between nvidia-smi's 200 ms samples); nvidia-smi is the
+    fallback when NVML is unavailable. Only samples taken while the GPU reports activity
+    (not the GpuIdle reason) count.
+    """
+
+    NAMES = {"hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+             "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+             "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+             "sw_power_cap": "nvmlClocksEventReasonSwPowerCap",
+             "hw_power_brake": "nvmlClocksEventReasonHwPowerBrakeSlowdown"}
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
-        self.path = None
+        self.samples = []  # (sm_mhz, reasons bitmask)
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
 
     def __enter__(self):
-        fd, self.path = tempfile.mkstemp(suffix=".csv")
-        os.close(fd)
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
-        except OSError:
-            self.proc = None
-        time.sleep(0.3)
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+
+            def loop():
+                while not self._stop.is_set():
+                    try:
+                        mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.samples.append((mhz, rs))
+                    except Exception:
+                        pass
+                    time.sleep(0.001)
+
+            self._thread = threading.Thread(target=loop, daemon=True)
+            self._thread.start()
+        except Exception:
+            self._nvml = None
+        time.sleep(0.01)
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        try:
-            for line in open(self.path):
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 9:
-                    continue
-                try:
-                    sm.append(float(parts[1]))
-                    mx.append(float(parts[2]))
-                except ValueError:
-                    continue
-                for n, v in zip(names, parts[5:9]):
-                    if v.lower() == "active":
-                        reasons.add(n)
-        finally:
-            os.unlink(self.path)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if self._nvml is None or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
+        pm = self._nvml
+        idle = getattr(pm, "nvmlClocksEventReasonGpuIdle", 1)
+        busy = [(m, r) for m, r in self.samples if not (r & idle)] or self.samples
+        reasons = sorted(n for n, attr in self.NAMES.items()
+                         if any(r & getattr(pm, attr, 0) for _, r in busy))
+        return {"sm_mhz": statistics.median(m for m, _ in busy), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(busy), "source": "NVML, 1 ms"}
 
 
 # ------------------------------------------------------------------------------------------
@@ -330,31 +337,37 @@ def extra_ops(torch, T, peaks):
         emb = torch.cat([torch.outer(pos, inv)] * 2, dim=-1)
         cos, sin = emb.cos().half(), emb.sin().half()
         nbytes = 2 * (b * s * h * d * 2) + d * 2 + 2 * (s * d * 2)
-        ts = _events_time(torch, lambda: T.rmsnorm_rope(x, w, cos, sin), 20, 5, flush)
+        with ClockSampler(torch.cuda.current_device()) as clk:
+            ts = _events_time(torch, lambda: T.rmsnorm_rope(x, w, cos, sin), 20, 5, flush)
         t = statistics.median(ts)
         gbs = nbytes / (t * 1e-3) / 1e9
         res[name] = {"value": gbs, "unit": "GB/s", "ms": t, "bytes": nbytes,
-                     "roofline_frac": gbs / hbm, "bound": "hbm", "l2": "flushed"}
+                     "roofline_frac": gbs / hbm, "bound": "hbm", "l2": "flushed",
+                     "sm_mhz": clk.summary().get("sm_mhz")}
         del x
     # flash_attention: causal [4,32,4096,128] and non-causal [4,32,1024,128].
     for name, (b, h, s, d), causal in [("flash_causal_4x32x4096x128", (4, 32, 4096, 128), True),
                                        ("flash_full_4x32x1024x128", (4, 32, 1024, 128), False)]:
         q, k, v = gen((b, h, s, d), 2), gen((b, h, s, d), 3), gen((b, h, s, d), 4)
         flops = 4.0 * b * h * s * s * d * (0.5 if causal else 1.0)
-        ts = _events_time(torch, lambda: T.flash_attention(q, k, v, causal=causal), 10, 3, flush)
+        with ClockSampler(torch.cuda.current_device()) as clk:
+            ts = _events_time(torch, lambda: T.flash_attention(q, k, v, causal=causal), 10, 3, flush)
         t = statistics.median(ts)
         tf = flops / (t * 1e-3) / 1e12
         res[name] = {"value": tf, "unit": "TFLOP/s", "ms": t, "flops": flops,
-                     "roofline_frac": tf / tc, "bound": "tensor"}
+                     "roofline_frac": tf / tc, "bound": "tensor",
+                     "sm_mhz": clk.summary().get("sm_mhz")}
         del q, k, v
     # paged_attention decode: B64 H32 D128 bs16, lens U[512,8192] (seed 3).
     qd, kc, vc, btd, cl, nbytes = _paged_inputs(torch, 64)
-    ts = _events_time(torch, lambda: T.paged_attention(qd, kc, vc, btd, cl, block_size=16), 20, 5, flush)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ts = _events_time(torch, lambda: T.paged_attention(qd, kc, vc, btd, cl, block_size=16), 20, 5, flush)
     t = statistics.median(ts)
     gbs = nbytes / (t * 1e-3) / 1e9
     res["paged_decode_b64_h32_d128_bs16"] = {"value": gbs, "unit": "GB/s", "ms": t, "bytes": nbytes,
                                               "roofline_frac": gbs / hbm, "bound": "hbm",
-                                              "kv_tokens": int(cl.sum().item())}
+                                              "kv_tokens": int(cl.sum().item()),
+                                              "sm_mhz": clk.summary().get("sm_mhz")}
     del kc, vc
     torch.cuda.empty_cache()
     return res
