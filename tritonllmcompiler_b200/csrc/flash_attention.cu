@@ -23,6 +23,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <type_traits>
 
 #include "common.h"
@@ -91,6 +92,8 @@ struct Args {
   float scale_log2;
   int causal;
   int vec_store;
+  int group;    // heads per scheduling group of the two-tile kernel (see pp_item)
+  int n_small;  // groups of `group` heads; the rest have group + 1
 };
 
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[32]) { tmem_ld32(taddr, r); }
@@ -404,14 +407,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 // =======================================================================================
 constexpr int kPPThreads = 384;
 constexpr int kPPSoftmaxWarp0 = 4;
-// Register hand-off (setmaxnreg): warps 0-3 (TMA, UMMA, two spare) keep 56, the two softmax
-// warpgroups get 224; 56 * 128 + 224 * 256 = 168 * 384, the launch budget.
+// Register hand-off (setmaxnreg): warps 0-3 (TMA, UMMA, two spare) keep 88, enough for the
+// fully unrolled UMMA issue loops of the work-stealing kernel without spills; the two softmax
+// warpgroups get 208; 88 * 128 + 208 * 256 = 168 * 384, the launch budget.
 constexpr int kPPRegsLaunch = 168;
-constexpr int kPPRegsLow = 56;
-constexpr int kPPRegsHigh = 224;
+constexpr int kPPRegsLow = 88;
+constexpr int kPPRegsHigh = 208;
 static_assert(kPPRegsLow * 128 + kPPRegsHigh * 256 <= kPPRegsLaunch * kPPThreads,
               "setmaxnreg split exceeds the launch register budget");
 constexpr float kLazyRescaleLog2 = 8.0f;
+constexpr int kGroupHeads = 8;
 
 
 template <int D>
@@ -428,9 +433,63 @@ struct GeoPP {
   static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
 };
 
-enum : int { SITE_PFULL = 9, SITE_ODONE = 10 };
+enum : int { SITE_PFULL = 9, SITE_ODONE = 10, SITE_QEMPTY = 11, SITE_CLC = 12 };
 
-template <typename T, int D>
+// One work item of the two-tile kernel: query rows [q0, q0 + 2*BM) of head (b, h) and the
+// number of key tiles each of its two query tiles visits.
+struct PPItem {
+  int b, h, q0;
+  int nkv[2];
+  int n_kv;
+};
+
+// Items are numbered in groups of consecutive (b, h) heads: a.n_small groups of a.group
+// heads, then groups of a.group + 1 heads (the last groups are the largest). Within a group
+// the heaviest causal pairs of every head come first, then the next heaviest, and so on.
+// Dynamic scheduling in that order ends each group, and the grid, with the lightest items (a
+// short tail), while the CTAs running at the same time read the K/V of only a few heads
+// (they stay in L2).
+__device__ __forceinline__ PPItem pp_item(const Args &a, int item) {
+  PPItem w;
+  const int n_pairs = (a.n_qtiles + 1) / 2;
+  const int small_items = a.n_small * a.group * n_pairs;
+  int heads = a.group, bh0 = 0, r = item;
+  if (item < small_items) {
+    const int grp = item / (heads * n_pairs);
+    r = item - grp * heads * n_pairs;
+    bh0 = grp * heads;
+  } else {
+    heads = a.group + 1;
+    const int grp = (item - small_items) / (heads * n_pairs);
+    r = item - small_items - grp * heads * n_pairs;
+    bh0 = a.n_small * a.group + grp * heads;
+  }
+  const int bh = bh0 + r % heads;
+  w.b = bh / a.H;
+  w.h = bh % a.H;
+  w.q0 = (n_pairs - 1 - r / heads) * 2 * BM;
+  const int kv_tiles_all = (a.Sk + BN - 1) / BN;
+#pragma unroll
+  for (int X = 0; X < 2; ++X) {
+    const int qx0 = w.q0 + X * BM;
+    int n = qx0 < a.Sq ? kv_tiles_all : 0;
+    if (a.causal && n > 0) n = min(n, (min(qx0 + BM, a.Sq) - 1) / BN + 1);
+    w.nkv[X] = n;
+  }
+  w.n_kv = max(w.nkv[0], w.nkv[1]);
+  return w;
+}
+
+// Readers of each work-stealing response: the UMMA lane and one lane per softmax warp.
+constexpr int kClcReaders = 1 + 8;
+
+// kSteal: the CTA keeps its TMEM, barriers and descriptors and moves on to further items. While
+// an item's last key/value tiles are in flight, the producer cancels the launch of the next CTA
+// that has not started (cluster launch control) and the CTA takes over that CTA's item, so
+// items still run in launch order, each on the first SM to free up, without a CTA launch and
+// set-up between them; the next item's Q tiles, first key tiles and first S overlap the
+// current item's epilogue.
+template <typename T, int D, bool kSteal>
 __global__ void __launch_bounds__(kPPThreads, 1)
     flash_pp_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
@@ -443,39 +502,26 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + G::BAR_OFF);
   uint64_t *q_full = bars + 0;
-  uint64_t *k_full = bars + 1;   // [2]
-  uint64_t *k_empty = bars + 3;  // [2]
-  uint64_t *v_full = bars + 5;   // [2]
-  uint64_t *v_empty = bars + 7;  // [2]
-  uint64_t *s_full = bars + 9;   // [2] per tile
-  uint64_t *p_full = bars + 11;  // [2] per tile
-  uint64_t *o_done = bars + 13;  // [2] per tile
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 15);
+  uint64_t *k_full = bars + 1;     // [2]
+  uint64_t *k_empty = bars + 3;    // [2]
+  uint64_t *v_full = bars + 5;     // [2]
+  uint64_t *v_empty = bars + 7;    // [2]
+  uint64_t *s_full = bars + 9;     // [2] per tile
+  uint64_t *p_full = bars + 11;    // [2] per tile
+  uint64_t *o_done = bars + 13;    // [2] per tile
+  uint64_t *q_empty = bars + 15;
+  uint64_t *clc_full = bars + 16;  // [2] per response slot
+  uint64_t *clc_empty = bars + 18; // [2] per response slot
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 20);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+  const uint32_t clc_resp = smem_u32(bars + 22);  // two 16-byte responses
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // 1-D grid, head-major (a head's query-tile pairs are adjacent in launch order, so the
-  // resident CTAs share few heads' K/V in L2), heaviest causal pairs first.
-  const int n_pairs = (a.n_qtiles + 1) / 2;
-  const int bh = static_cast<int>(blockIdx.x / n_pairs);
-  const int b = bh / a.H;
-  const int h = bh % a.H;
-  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.x % n_pairs);
-  const int q0 = pair * 2 * BM;
-  const int kv_tiles_all = (a.Sk + BN - 1) / BN;
-  int nkv[2];
-#pragma unroll
-  for (int X = 0; X < 2; ++X) {
-    const int qx0 = q0 + X * BM;
-    int n = qx0 < a.Sq ? kv_tiles_all : 0;
-    if (a.causal && n > 0) n = min(n, (min(qx0 + BM, a.Sq) - 1) / BN + 1);
-    nkv[X] = n;
-  }
-  const int n_kv = max(nkv[0], nkv[1]);
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(q_full), 1);
+    mbar_init(smem_u32(q_empty), 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(smem_u32(&k_full[s]), 1);
       mbar_init(smem_u32(&k_empty[s]), 1);
@@ -484,6 +530,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       mbar_init(smem_u32(&s_full[s]), 1);
       mbar_init(smem_u32(&p_full[s]), kSoftmaxThreads);
       mbar_init(smem_u32(&o_done[s]), 1);
+      mbar_init(smem_u32(&clc_full[s]), 1);
+      mbar_init(smem_u32(&clc_empty[s]), kClcReaders);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -502,51 +550,93 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   const uint32_t sQ = smem_u32(smem + G::Q_OFF);
   const uint32_t sK = smem_u32(smem + G::K_OFF);
   const uint32_t sV = smem_u32(smem + G::V_OFF);
+  // Waits for the response to the request made during the it-th item and returns the next
+  // item (-1: the grid is exhausted; -2: a wait gave up). With warp_vote the whole warp calls
+  // it and gets the same answer.
+  auto read_next = [&](int it, bool warp_vote) -> int {
+    const int slot = it & 1;
+    bool got = mbar_wait(smem_u32(&clc_full[slot]), (it >> 1) & 1, abort_flag, &g_flash_status,
+                         TLLM_DEV_WAIT_TIMEOUT + SITE_CLC);
+    if (warp_vote) got = __all_sync(0xffffffffu, got);
+    if (!got) return -2;
+    const int nxt = clc_cancelled_ctaid_x(clc_resp + 16 * slot);
+    // The slot is rewritten by the async proxy two items later.
+    fence_proxy_async_smem();
+    return nxt;
+  };
   if (warp < kPPSoftmaxWarp0) {
   regs_dec<kPPRegsLow>();
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
-    if (lane == 0 && n_kv > 0) {
-      const uint32_t qb = smem_u32(q_full);
-      mbar_arrive_expect_tx(qb, G::TILE_BYTES * ((nkv[0] > 0) + (nkv[1] > 0)));
+    if (lane == 0) {
+      int item = static_cast<int>(blockIdx.x);
+      int g = 0;   // key/value tiles loaded so far (ring position)
+      int nq = 0;  // Q loads so far
+      bool ok = true;
+      for (int it = 0; ok && item >= 0; ++it) {
+        const PPItem w = pp_item(a, item);
+        if (w.n_kv > 0) {
+          // The previous item's last QK has read its Q tiles.
+          if (nq > 0 && !mbar_wait(smem_u32(q_empty), (nq - 1) & 1, abort_flag, &g_flash_status,
+                                   TLLM_DEV_WAIT_TIMEOUT + SITE_QEMPTY))
+            break;
+          const uint32_t qb = smem_u32(q_full);
+          mbar_arrive_expect_tx(qb, G::TILE_BYTES * ((w.nkv[0] > 0) + (w.nkv[1] > 0)));
 #pragma unroll
-      for (int X = 0; X < 2; ++X) {
-        if (nkv[X] == 0) continue;
+          for (int X = 0; X < 2; ++X) {
+            if (w.nkv[X] == 0) continue;
 #pragma unroll
-        for (int c = 0; c < G::CHUNKS; ++c)
-          tma_load_4d(sQ + X * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_q, qb, c * (G::SWB / 2),
-                      q0 + X * BM, h, b);
-      }
-      for (int j = 0; j < n_kv; ++j) {
-        const int s = j & 1;
-        const uint32_t par = ((j >> 1) & 1) ^ 1;
-        if (!mbar_wait(smem_u32(&k_empty[s]), par, abort_flag, &g_flash_status,
-                       TLLM_DEV_WAIT_TIMEOUT + SITE_KEMPTY))
+            for (int c = 0; c < G::CHUNKS; ++c)
+              tma_load_4d(sQ + X * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_q, qb,
+                          c * (G::SWB / 2), w.q0 + X * BM, w.h, w.b);
+          }
+          ++nq;
+          for (int j = 0; j < w.n_kv; ++j, ++g) {
+            const int s = g & 1;
+            const uint32_t par = ((g >> 1) & 1) ^ 1;
+            if (!mbar_wait(smem_u32(&k_empty[s]), par, abort_flag, &g_flash_status,
+                           TLLM_DEV_WAIT_TIMEOUT + SITE_KEMPTY)) {
+              ok = false;
+              break;
+            }
+            const uint32_t kb = smem_u32(&k_full[s]);
+            mbar_arrive_expect_tx(kb, G::TILE_BYTES);
+#pragma unroll
+            for (int c = 0; c < G::CHUNKS; ++c)
+              tma_load_4d(sK + s * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_k, kb,
+                          c * (G::SWB / 2), j * BN, w.h, w.b);
+            if (!mbar_wait(smem_u32(&v_empty[s]), par, abort_flag, &g_flash_status,
+                           TLLM_DEV_WAIT_TIMEOUT + SITE_VEMPTY)) {
+              ok = false;
+              break;
+            }
+            const uint32_t vb = smem_u32(&v_full[s]);
+            mbar_arrive_expect_tx(vb, G::TILE_BYTES);
+#pragma unroll
+            for (int c = 0; c < G::CHUNKS; ++c)
+              tma_load_4d(sV + s * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_v, vb,
+                          c * (G::SWB / 2), j * BN, w.h, w.b);
+          }
+        }
+        if (!ok || !kSteal) break;
+        // Claim the next item while this one's last tiles are in flight.
+        const int slot = it & 1;
+        if (it >= 2 && !mbar_wait(smem_u32(&clc_empty[slot]), ((it >> 1) - 1) & 1, abort_flag,
+                                  &g_flash_status, TLLM_DEV_WAIT_TIMEOUT + SITE_CLC))
           break;
-        const uint32_t kb = smem_u32(&k_full[s]);
-        mbar_arrive_expect_tx(kb, G::TILE_BYTES);
-#pragma unroll
-        for (int c = 0; c < G::CHUNKS; ++c)
-          tma_load_4d(sK + s * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_k, kb, c * (G::SWB / 2),
-                      j * BN, h, b);
-        if (!mbar_wait(smem_u32(&v_empty[s]), par, abort_flag, &g_flash_status,
-                       TLLM_DEV_WAIT_TIMEOUT + SITE_VEMPTY))
-          break;
-        const uint32_t vb = smem_u32(&v_full[s]);
-        mbar_arrive_expect_tx(vb, G::TILE_BYTES);
-#pragma unroll
-        for (int c = 0; c < G::CHUNKS; ++c)
-          tma_load_4d(sV + s * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_v, vb, c * (G::SWB / 2),
-                      j * BN, h, b);
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(smem_u32(&clc_full[slot]), 16);
+        clc_try_cancel(clc_resp + 16 * slot, smem_u32(&clc_full[slot]));
+        item = read_next(it, false);
       }
     }
   } else if (warp == 1) {
     // ------------------------------ UMMA issuer -------------------------------
-    if (lane == 0 && n_kv > 0) {
+    if (lane == 0) {
       const uint32_t idesc_qk = make_idesc_f16(BM, BN, kBF16, false, false);
       const uint32_t idesc_pv = make_idesc_f16(BM, D, kBF16, false, true);
-      auto issue_qk = [&](int X, int j) {
-        const uint32_t kbase = sK + (j & 1) * G::TILE_BYTES;
+      auto issue_qk = [&](int X, int kslot) {
+        const uint32_t kbase = sK + kslot * G::TILE_BYTES;
         const uint32_t qbase = sQ + X * G::TILE_BYTES;
 #pragma unroll
         for (int k = 0; k < D / 16; ++k)
@@ -554,61 +644,82 @@ __global__ void __launch_bounds__(kPPThreads, 1)
                       idesc_qk, k != 0 ? 1u : 0u);
         umma_commit(smem_u32(&s_full[X]));
       };
-      bool ok = mbar_wait(smem_u32(q_full), 0, abort_flag, &g_flash_status,
-                          TLLM_DEV_WAIT_TIMEOUT + SITE_Q) &&
-                mbar_wait(smem_u32(&k_full[0]), 0, abort_flag, &g_flash_status,
-                          TLLM_DEV_WAIT_TIMEOUT + SITE_KFULL);
-      if (ok) {
-        tc_fence_after();
-#pragma unroll
-        for (int X = 0; X < 2; ++X)
-          if (nkv[X] > 0) issue_qk(X, 0);
-        umma_commit(smem_u32(&k_empty[0]));
-      }
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(smem_u32(&v_full[s]), (j >> 1) & 1, abort_flag, &g_flash_status,
-                       TLLM_DEV_WAIT_TIMEOUT + SITE_VFULL)) {
-          ok = false;
-          break;
-        }
-        const uint32_t vbase = sV + s * G::TILE_BYTES;
-        bool next_k_ready = false;
-#pragma unroll
-        for (int X = 0; X < 2; ++X) {
-          if (j >= nkv[X]) continue;
-          if (!mbar_wait(smem_u32(&p_full[X]), j & 1, abort_flag, &g_flash_status,
-                         TLLM_DEV_WAIT_TIMEOUT + SITE_PFULL)) {
-            ok = false;
-            break;
-          }
+      int item = static_cast<int>(blockIdx.x);
+      int g = 0, nq = 0;
+      uint32_t npf[2] = {0u, 0u};  // P tiles consumed per query tile
+      bool ok = true;
+      for (int it = 0; ok && item >= 0; ++it) {
+        const PPItem w = pp_item(a, item);
+        if (w.n_kv > 0) {
+          ok = mbar_wait(smem_u32(q_full), nq & 1, abort_flag, &g_flash_status,
+                         TLLM_DEV_WAIT_TIMEOUT + SITE_Q) &&
+               mbar_wait(smem_u32(&k_full[g & 1]), (g >> 1) & 1, abort_flag, &g_flash_status,
+                         TLLM_DEV_WAIT_TIMEOUT + SITE_KFULL);
+          ++nq;
+          if (!ok) break;
+          // S_X of the previous item was last read as P by its final PV, issued before this
+          // QK; its O_X was read out by the epilogue before the softmax signalled this item's
+          // first P, which the first PV below waits for.
           tc_fence_after();
-          const uint32_t p_tmem = tmem_base + X * BN;
-          const uint32_t o_tmem = tmem_base + O_COL + X * BN;
 #pragma unroll
-          for (int k = 0; k < BN / 16; ++k) {
-            const uint64_t bdesc =
-                make_sdesc(vbase + k * 16 * G::SWB, G::CHUNK_BYTES, 8 * G::SWB, G::LAYOUT);
-            umma_f16_ts(o_tmem, p_tmem + k * 8, bdesc, idesc_pv, (j | k) != 0 ? 1u : 0u);
-          }
-          if (j == nkv[X] - 1) {
-            umma_commit(smem_u32(&o_done[X]));
-          } else {
-            if (!next_k_ready) {
-              if (!mbar_wait(smem_u32(&k_full[(j + 1) & 1]), ((j + 1) >> 1) & 1, abort_flag,
-                             &g_flash_status, TLLM_DEV_WAIT_TIMEOUT + SITE_KFULL)) {
+          for (int X = 0; X < 2; ++X)
+            if (w.nkv[X] > 0) issue_qk(X, g & 1);
+          umma_commit(smem_u32(&k_empty[g & 1]));
+          if (w.n_kv == 1) umma_commit(smem_u32(q_empty));
+          for (int j = 0; j < w.n_kv && ok; ++j) {
+            const int gj = g + j;
+            const int s = gj & 1;
+            if (!mbar_wait(smem_u32(&v_full[s]), (gj >> 1) & 1, abort_flag, &g_flash_status,
+                           TLLM_DEV_WAIT_TIMEOUT + SITE_VFULL)) {
+              ok = false;
+              break;
+            }
+            const uint32_t vbase = sV + s * G::TILE_BYTES;
+            bool next_k_ready = false;
+#pragma unroll
+            for (int X = 0; X < 2; ++X) {
+              if (j >= w.nkv[X]) continue;
+              if (!mbar_wait(smem_u32(&p_full[X]), npf[X] & 1, abort_flag, &g_flash_status,
+                             TLLM_DEV_WAIT_TIMEOUT + SITE_PFULL)) {
                 ok = false;
                 break;
               }
+              ++npf[X];
               tc_fence_after();
-              next_k_ready = true;
+              const uint32_t p_tmem = tmem_base + X * BN;
+              const uint32_t o_tmem = tmem_base + O_COL + X * BN;
+#pragma unroll
+              for (int k = 0; k < BN / 16; ++k) {
+                const uint64_t bdesc =
+                    make_sdesc(vbase + k * 16 * G::SWB, G::CHUNK_BYTES, 8 * G::SWB, G::LAYOUT);
+                umma_f16_ts(o_tmem, p_tmem + k * 8, bdesc, idesc_pv, (j | k) != 0 ? 1u : 0u);
+              }
+              if (j == w.nkv[X] - 1) {
+                umma_commit(smem_u32(&o_done[X]));
+              } else {
+                if (!next_k_ready) {
+                  if (!mbar_wait(smem_u32(&k_full[(gj + 1) & 1]), ((gj + 1) >> 1) & 1, abort_flag,
+                                 &g_flash_status, TLLM_DEV_WAIT_TIMEOUT + SITE_KFULL)) {
+                    ok = false;
+                    break;
+                  }
+                  tc_fence_after();
+                  next_k_ready = true;
+                }
+                issue_qk(X, (gj + 1) & 1);
+              }
             }
-            issue_qk(X, j + 1);
+            if (!ok) break;
+            umma_commit(smem_u32(&v_empty[s]));
+            if (next_k_ready) umma_commit(smem_u32(&k_empty[(gj + 1) & 1]));
+            // The item's last QK has been issued: its Q tiles are free once it completes.
+            if (j == w.n_kv - 2) umma_commit(smem_u32(q_empty));
           }
+          g += w.n_kv;
         }
-        if (!ok) break;
-        umma_commit(smem_u32(&v_empty[s]));
-        if (next_k_ready) umma_commit(smem_u32(&k_empty[(j + 1) & 1]));
+        if (!ok || !kSteal) break;
+        item = read_next(it, false);
+        if (item >= -1) mbar_arrive(smem_u32(&clc_empty[it & 1]));
       }
     }
   }
@@ -618,131 +729,151 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     const int X = (warp - kPPSoftmaxWarp0) >> 2;
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
-    const int qx0 = q0 + X * BM;
-    const int qg = qx0 + row;
-    const int nk = nkv[X];
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t s_tm = tmem_base + lane_off + X * BN;
     const uint32_t o_tm = tmem_base + lane_off + O_COL + X * BN;
-    float m_use = -INFINITY;  // max the exponentials are taken against (lazily updated)
-    float l_run = 0.f;
+    int item = static_cast<int>(blockIdx.x);
+    uint32_t ns = 0;   // S tiles consumed
+    uint32_t nod = 0;  // O tiles finished
     bool ok = true;
-    for (int j = 0; j < nk; ++j) {
-      if (!mbar_wait(smem_u32(&s_full[X]), j & 1, abort_flag, &g_flash_status,
-                     TLLM_DEV_WAIT_TIMEOUT + SITE_SFULL)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const int k0 = j * BN;
-      const bool need_mask = (k0 + BN > a.Sk) || (a.causal && k0 + BN - 1 > qx0);
-      // The whole S row in one TMEM round trip (four 32-column loads, one wait).
-      uint32_t sr[BN];
-      tmem_ld4x32(s_tm, sr);
-      if (need_mask) {
-#pragma unroll
-        for (int t = 0; t < BN; ++t) {
-          const int kg = k0 + t;
-          if (kg >= a.Sk || (a.causal && kg > qg)) sr[t] = __float_as_uint(-INFINITY);
+    for (int it = 0; ok && item >= 0; ++it) {
+      const PPItem w = pp_item(a, item);
+      const int qx0 = w.q0 + X * BM;
+      const int qg = qx0 + row;
+      const int nk = w.nkv[X];
+      float m_use = -INFINITY;  // max the exponentials are taken against (lazily updated)
+      float l_run = 0.f;
+      for (int j = 0; j < nk; ++j, ++ns) {
+        // Waits are voted warp-wide so that a warp leaves together even when a wait gives up.
+        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&s_full[X]), ns & 1, abort_flag,
+                                               &g_flash_status, TLLM_DEV_WAIT_TIMEOUT + SITE_SFULL))) {
+          ok = false;
+          break;
         }
-      }
-      // Row max on the raw scores (the scale is positive): an 8-way tree of 3-input maxima.
-      float mx8[8];
+        tc_fence_after();
+        const int k0 = j * BN;
+        const bool need_mask = (k0 + BN > a.Sk) || (a.causal && k0 + BN - 1 > qx0);
+        // The whole S row in one TMEM round trip (four 32-column loads, one wait).
+        uint32_t sr[BN];
+        tmem_ld4x32(s_tm, sr);
+        if (need_mask) {
 #pragma unroll
-      for (int t = 0; t < 8; ++t) mx8[t] = __uint_as_float(sr[t]);
-#pragma unroll
-      for (int t = 8; t < BN; t += 2)
-        mx8[(t >> 1) & 7] = max3f(mx8[(t >> 1) & 7], __uint_as_float(sr[t]), __uint_as_float(sr[t + 1]));
-      float mx = max3f(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], mx8[5]),
-                       fmaxf(mx8[6], mx8[7]));
-      mx *= a.scale_log2;
-      float alpha = 1.0f;
-      bool rescale = false;
-      if (m_use == -INFINITY) {
-        m_use = mx;  // first tile: O not written yet, nothing to rescale
-      } else if (mx > m_use + kLazyRescaleLog2) {
-        alpha = ex2_approx(m_use - mx);
-        m_use = mx;
-        rescale = true;
-      }
-      const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
-      // P = 2^(s * scale - m), packed in pairs over S's first 64 columns (S's values are all
-      // in registers by now).
-      // Exponent arguments and the row sum use packed fp32 pairs (one instruction per pair).
-      const uint64_t scale2 = f2_pack(a.scale_log2, a.scale_log2);
-      const uint64_t negm2 = f2_pack(neg_m, neg_m);
-      uint64_t ps2[4] = {0ull, 0ull, 0ull, 0ull};
-#pragma unroll
-      for (int hlf = 0; hlf < 2; ++hlf) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int t = 0; t < 64; t += 2) {
-          const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sr[64 * hlf + t]), __uint_as_float(sr[64 * hlf + t + 1])),
-                                     scale2, negm2);
-          float x0, x1;
-          f2_unpack(x2, x0, x1);
-          const float p0 = ex2_approx(x0);
-          const float p1 = ex2_approx(x1);
-          ps2[(t >> 1) & 3] = f2_add(ps2[(t >> 1) & 3], f2_pack(p0, p1));
-          pk[t >> 1] = Pack2<T>::pack(p0, p1);
+          for (int t = 0; t < BN; ++t) {
+            const int kg = k0 + t;
+            if (kg >= a.Sk || (a.causal && kg > qg)) sr[t] = __float_as_uint(-INFINITY);
+          }
         }
-        tmem_st32(s_tm + 32 * hlf, pk);
+        // Row max on the raw scores (the scale is positive): an 8-way tree of 3-input maxima.
+        float mx8[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) mx8[t] = __uint_as_float(sr[t]);
+#pragma unroll
+        for (int t = 8; t < BN; t += 2)
+          mx8[(t >> 1) & 7] =
+              max3f(mx8[(t >> 1) & 7], __uint_as_float(sr[t]), __uint_as_float(sr[t + 1]));
+        float mx = max3f(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], mx8[5]),
+                         fmaxf(mx8[6], mx8[7]));
+        mx *= a.scale_log2;
+        float alpha = 1.0f;
+        bool rescale = false;
+        if (m_use == -INFINITY) {
+          m_use = mx;  // first tile: O not written yet, nothing to rescale
+        } else if (mx > m_use + kLazyRescaleLog2) {
+          alpha = ex2_approx(m_use - mx);
+          m_use = mx;
+          rescale = true;
+        }
+        const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
+        // P = 2^(s * scale - m), written over S's first 64 columns in packed pairs (S's values
+        // are all in registers by now). Exponent arguments and the row sum use packed fp32
+        // pairs (one instruction per pair).
+        const uint64_t scale2 = f2_pack(a.scale_log2, a.scale_log2);
+        const uint64_t negm2 = f2_pack(neg_m, neg_m);
+        uint64_t ps2[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+        for (int hlf = 0; hlf < 2; ++hlf) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int t = 0; t < 64; t += 2) {
+            const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sr[64 * hlf + t]),
+                                               __uint_as_float(sr[64 * hlf + t + 1])),
+                                       scale2, negm2);
+            float x0, x1;
+            f2_unpack(x2, x0, x1);
+            const float p0 = ex2_approx(x0);
+            const float p1 = ex2_approx(x1);
+            ps2[(t >> 1) & 3] = f2_add(ps2[(t >> 1) & 3], f2_pack(p0, p1));
+            pk[t >> 1] = Pack2<T>::pack(p0, p1);
+          }
+          tmem_st32(s_tm + 32 * hlf, pk);
+        }
+        float psa, psb, psc, psd, pse, psf, psg, psh;
+        f2_unpack(ps2[0], psa, psb);
+        f2_unpack(ps2[1], psc, psd);
+        f2_unpack(ps2[2], pse, psf);
+        f2_unpack(ps2[3], psg, psh);
+        const float psum = ((psa + psb) + (psc + psd)) + ((pse + psf) + (psg + psh));
+        l_run = l_run * alpha + psum;
+        // O_X is stable here: PV_X(j-1) was issued before QK_X(j), whose completion s_full
+        // signalled.
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+          for (int c = 0; c < D; c += OC) {
+            uint32_t r[OC];
+            tmem_ld_cols(o_tm + c, r);
+#pragma unroll
+            for (int t = 0; t < OC; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * alpha);
+            tmem_st_cols(o_tm + c, r);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(smem_u32(&p_full[X]));
       }
-      float psa, psb, psc, psd, pse, psf, psg, psh;
-      f2_unpack(ps2[0], psa, psb);
-      f2_unpack(ps2[1], psc, psd);
-      f2_unpack(ps2[2], pse, psf);
-      f2_unpack(ps2[3], psg, psh);
-      const float psum = ((psa + psb) + (psc + psd)) + ((pse + psf) + (psg + psh));
-      l_run = l_run * alpha + psum;
-      // O_X is stable here: PV_X(j-1) was issued before QK_X(j), whose completion s_full
-      // signalled.
-      if (__any_sync(0xffffffffu, rescale)) {
+      if (!ok) break;
+      // ---- epilogue: O / l -> global ----
+      if (nk > 0) {
+        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&o_done[X]), nod & 1, abort_flag,
+                                               &g_flash_status, TLLM_DEV_WAIT_TIMEOUT + SITE_ODONE)))
+          break;
+        ++nod;
+        tc_fence_after();
+        const float inv_l = 1.0f / l_run;
+        T *orow = static_cast<T *>(a.o) + w.b * a.so0 + w.h * a.so1 +
+                  static_cast<int64_t>(qg) * a.so2;
 #pragma unroll 1
         for (int c = 0; c < D; c += OC) {
           uint32_t r[OC];
           tmem_ld_cols(o_tm + c, r);
+          if (qg < a.Sq) {
+            if (a.vec_store) {
 #pragma unroll
-          for (int t = 0; t < OC; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * alpha);
-          tmem_st_cols(o_tm + c, r);
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(smem_u32(&p_full[X]));
-    }
-    // ---- epilogue: O / l -> global ----
-    if (ok && nk > 0 &&
-        mbar_wait(smem_u32(&o_done[X]), 0, abort_flag, &g_flash_status,
-                  TLLM_DEV_WAIT_TIMEOUT + SITE_ODONE)) {
-      tc_fence_after();
-      const float inv_l = 1.0f / l_run;
-      T *orow = static_cast<T *>(a.o) + b * a.so0 + h * a.so1 + static_cast<int64_t>(qg) * a.so2;
-#pragma unroll 1
-      for (int c = 0; c < D; c += OC) {
-        uint32_t r[OC];
-        tmem_ld_cols(o_tm + c, r);
-        if (qg < a.Sq) {
-          if (a.vec_store) {
+              for (int t = 0; t < OC; t += 8) {
+                uint4 pk;
+                pk.x = Pack2<T>::pack(__uint_as_float(r[t + 0]) * inv_l, __uint_as_float(r[t + 1]) * inv_l);
+                pk.y = Pack2<T>::pack(__uint_as_float(r[t + 2]) * inv_l, __uint_as_float(r[t + 3]) * inv_l);
+                pk.z = Pack2<T>::pack(__uint_as_float(r[t + 4]) * inv_l, __uint_as_float(r[t + 5]) * inv_l);
+                pk.w = Pack2<T>::pack(__uint_as_float(r[t + 6]) * inv_l, __uint_as_float(r[t + 7]) * inv_l);
+                *reinterpret_cast<uint4 *>(orow + c + t) = pk;
+              }
+            } else {
 #pragma unroll
-            for (int t = 0; t < OC; t += 8) {
-              uint4 pk;
-              pk.x = Pack2<T>::pack(__uint_as_float(r[t + 0]) * inv_l, __uint_as_float(r[t + 1]) * inv_l);
-              pk.y = Pack2<T>::pack(__uint_as_float(r[t + 2]) * inv_l, __uint_as_float(r[t + 3]) * inv_l);
-              pk.z = Pack2<T>::pack(__uint_as_float(r[t + 4]) * inv_l, __uint_as_float(r[t + 5]) * inv_l);
-              pk.w = Pack2<T>::pack(__uint_as_float(r[t + 6]) * inv_l, __uint_as_float(r[t + 7]) * inv_l);
-              *reinterpret_cast<uint4 *>(orow + c + t) = pk;
+              for (int t = 0; t < OC; ++t)
+                orow[(c + t) * a.so3] = from_f32<T>(__uint_as_float(r[t]) * inv_l);
             }
-          } else {
-#pragma unroll
-            for (int t = 0; t < OC; ++t)
-              orow[(c + t) * a.so3] = from_f32<T>(__uint_as_float(r[t]) * inv_l);
           }
         }
+        // The O_X reads above complete (tcgen05.wait::ld) before this warp's next P store,
+        // which the next item's first PV_X waits for.
+      } else if (qx0 < a.Sq && qg < a.Sq) {
+        // No keys at all (Sk == 0): 0/0, as in the reference.
+        T *orow = static_cast<T *>(a.o) + w.b * a.so0 + w.h * a.so1 +
+                  static_cast<int64_t>(qg) * a.so2;
+        for (int c = 0; c < D; ++c) orow[c * a.so3] = from_f32<T>(NAN);
       }
-    } else if (nk == 0 && qx0 < a.Sq && qg < a.Sq) {
-      // No keys at all (Sk == 0): 0/0, as in the reference.
-      T *orow = static_cast<T *>(a.o) + b * a.so0 + h * a.so1 + static_cast<int64_t>(qg) * a.so2;
-      for (int c = 0; c < D; ++c) orow[c * a.so3] = from_f32<T>(NAN);
+      if (!kSteal) break;
+      item = read_next(it, true);
+      __syncwarp();
+      if (lane == 0 && item >= -1) mbar_arrive(smem_u32(&clc_empty[it & 1]));
     }
   }
 
@@ -756,10 +887,12 @@ __global__ void __launch_bounds__(kPPThreads, 1)
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Kernel variants: the two-tile ping-pong kernel is the default; the single-tile kernel is
-// kept as a cross-check (tllm_flash_attn_fwd_variant).
+// Kernel variants (tllm_flash_attn_fwd_variant): the two-tile kernel with work stealing is
+// the default; the single-tile kernel and the two-tile kernel with one item per CTA are kept
+// as cross-checks.
 constexpr int kVariantPingPong = 0;
 constexpr int kVariantSingleTile = 1;
+constexpr int kVariantPingPongOneItem = 2;
 
 template <typename T, int D>
 int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, int64_t H,
@@ -801,6 +934,21 @@ int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, in
   a.scale_log2 = sm_scale * kLog2e;
   a.causal = causal ? 1 : 0;
   a.vec_store = (so[3] == 1 && so[0] % 8 == 0 && so[1] % 8 == 0 && so[2] % 8 == 0 && aligned16(o)) ? 1 : 0;
+  {
+    // Scheduling groups of the two-tile kernel: kGroupHeads heads per group, or all heads in
+    // one group when a causal grid is only a few waves long (its tail then comes from the
+    // lightest items of all heads); at most 64 MiB of K and V per group; sizes as even as
+    // possible.
+    const int64_t bh = B * H;
+    const int64_t n_pairs = (a.n_qtiles + 1) / 2;
+    const int64_t sms = sm_count() > 0 ? sm_count() : 148;
+    const int64_t kv_head_bytes = 2 * (Sk > 0 ? Sk : 1) * static_cast<int64_t>(D) * 2;
+    int64_t target = (causal && bh * n_pairs <= 4 * sms) ? bh : kGroupHeads;
+    target = std::min<int64_t>(target, std::max<int64_t>(1, (64ll << 20) / kv_head_bytes));
+    const int64_t n_groups = (bh + target - 1) / target;
+    a.group = static_cast<int>(bh / n_groups);
+    a.n_small = static_cast<int>(n_groups - bh % n_groups);
+  }
   if (variant == kVariantSingleTile) {
     auto kern = flash_fwd_kernel<T, D>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
@@ -810,7 +958,8 @@ int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, in
     return cuda_status(cudaGetLastError(), "flash launch");
   }
   using GP = GeoPP<D>;
-  auto kern = flash_pp_kernel<T, D>;
+  auto kern = variant == kVariantPingPongOneItem ? flash_pp_kernel<T, D, false>
+                                                 : flash_pp_kernel<T, D, true>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GP::SMEM_BYTES);
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(flash pp)");
   // setmaxnreg.inc only completes if the launch holds the registers the split assumes.
@@ -859,7 +1008,8 @@ int entry(const void *q, const void *k, const void *v, void *o, int64_t B, int64
                  "flash_attention: head dim %lld not in {16,32,64,128}", (long long)D);
   TLLM_CHECK_ARG(dtype == TLLM_DTYPE_F16 || dtype == TLLM_DTYPE_BF16,
                  "flash_attention: unsupported dtype %d", dtype);
-  TLLM_CHECK_ARG(variant == kVariantPingPong || variant == kVariantSingleTile,
+  TLLM_CHECK_ARG(variant == kVariantPingPong || variant == kVariantSingleTile ||
+                     variant == kVariantPingPongOneItem,
                  "flash_attention: unknown kernel variant %d", variant);
   TLLM_CHECK_ARG(sq && sk && sv && so, "flash_attention: null stride array");
   if (B == 0 || H == 0 || Sq == 0) return TLLM_OK;

@@ -391,6 +391,32 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   return d;
 }
 
+// Cluster launch control: asks the hardware to cancel the launch of a CTA that has not started
+// yet; the 16-byte response lands in shared memory at `resp` and completes 16 transaction
+// bytes on `bar`.
+__device__ __forceinline__ void clc_try_cancel(uint32_t resp, uint32_t bar) {
+  asm volatile(
+      "clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], "
+      "[%1];" ::"r"(resp),
+      "r"(bar)
+      : "memory");
+}
+// Decodes a response: the cancelled CTA's blockIdx.x, or -1 when no launch was cancelled.
+__device__ __forceinline__ int clc_cancelled_ctaid_x(uint32_t resp) {
+  uint32_t valid, x;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b128 r;\n\t"
+      "ld.shared.b128 r, [%2];\n\t"
+      "mov.u32 %1, 0;\n\t"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t"
+      "@p clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %1, r;\n\t}"
+      : "=r"(valid), "=r"(x)
+      : "r"(resp)
+      : "memory");
+  return valid ? static_cast<int>(x) : -1;
+}
+
 // ------------------------------------ numeric helpers ----------------------------------
 template <typename T>
 struct Pack2;
