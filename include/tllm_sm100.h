@@ -188,6 +188,71 @@ TLLM_API int tllm_ipc_get_handle(const void *ptr, void *handle_out, uint64_t *of
 TLLM_API int tllm_ipc_open(const void *handle, uint64_t offset, void **ptr_out, void **base_out);
 TLLM_API int tllm_ipc_close(void *base);
 
+/*
+ * Operators either side of decode (no counterpart in the reference, which only decodes from a
+ * paged cache: python/triton_llm/ops/paged_attention.py:92-128). They use its cache layout:
+ * token t of sequence b at cache[block_tables[b, t / block_size], t % block_size, h, :]
+ * (python/triton_llm/reference/paged_attention.py:29-37).
+ *
+ * tllm_paged_kv_append writes k_new/v_new [B, T, H, D] (strides skn/svn) into the caches
+ * [num_blocks, block_size, H, D] (strides skc/svc): token t of sequence b goes to position
+ * start_pos[b] + t, for t < n_new[b] (every t < T when n_new is NULL). block_tables is
+ * [B, max_blocks] int32 (strides sbt), start_pos and n_new are [B] int32, all on the device.
+ * A position past the block table or a table entry outside [0, num_blocks) is skipped and
+ * reported through tllm_debug_status (TLLM_DEV_BAD_INDEX). Inner strides must be 1, other
+ * strides multiples of 8 elements, pointers 16-byte aligned.
+ */
+TLLM_API int tllm_paged_kv_append(const void *k_new, const void *v_new, void *k_cache,
+                                  void *v_cache, const int32_t *block_tables,
+                                  const int32_t *start_pos, const int32_t *n_new, int64_t B,
+                                  int64_t T, int64_t H, int64_t D, int64_t block_size,
+                                  int64_t max_blocks, int64_t num_blocks, const int64_t *skn,
+                                  const int64_t *svn, const int64_t *skc, const int64_t *svc,
+                                  const int64_t *sbt, int dtype, void *stream);
+
+/*
+ * tllm_paged_kv_append with K passed through the fused RMSNorm + RoPE of tllm_rmsnorm_rope
+ * first (weight [D]; cos/sin [rope_rows, D] with row strides scos/ssin). The RoPE row of
+ * token t of sequence b is its absolute position start_pos[b] + t; a position at or past
+ * rope_rows is skipped and reported like a bad block index. The cache receives exactly
+ * what tllm_rmsnorm_rope returns for that row.
+ */
+TLLM_API int tllm_paged_kv_append_rope(const void *k_new, const void *v_new, const void *weight,
+                                       const void *cos, const void *sin, int64_t rope_rows,
+                                       int64_t scos, int64_t ssin, void *k_cache,
+                                       void *v_cache, const int32_t *block_tables,
+                                       const int32_t *start_pos, const int32_t *n_new,
+                                       int64_t B, int64_t T, int64_t H, int64_t D,
+                                       int64_t block_size, int64_t max_blocks,
+                                       int64_t num_blocks, const int64_t *skn,
+                                       const int64_t *svn, const int64_t *skc,
+                                       const int64_t *svc, const int64_t *sbt, float eps,
+                                       int dtype, void *stream);
+
+/*
+ * Attention of Sq >= 1 new query tokens per sequence over the paged cache, with grouped query
+ * heads: q [B, Hq, Sq, D] (strides sq), caches [num_blocks, block_size, Hkv, D] with
+ * Hq % Hkv == 0 (query head h reads KV head h / (Hq / Hkv)), output o [B, Hq, Sq, D]
+ * (strides so). context_lens[b] counts the new tokens (they are already in the cache); query
+ * token s sits at position context_lens[b] - Sq + s and, when causal != 0, sees the keys at
+ * positions <= its own (all context_lens[b] keys otherwise). A query that sees no key gives
+ * NaN. With Sq = 1 and Hq = Hkv this is tllm_paged_attn_decode. Requirements as for
+ * tllm_paged_attn_decode (block_size in {16,32,64}, D in {16,32,64,128}, unit inner strides,
+ * 16-byte alignment); the workspace (256-byte aligned) holds split-KV partials when a launch
+ * splits the keys (tllm_paged_prefill_workspace_size, 0 when it does not).
+ */
+TLLM_API size_t tllm_paged_prefill_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
+                                                  int64_t D, int64_t block_size,
+                                                  int64_t max_blocks);
+TLLM_API int tllm_paged_prefill(const void *q, const void *k_cache, const void *v_cache,
+                                const int32_t *block_tables, const int32_t *context_lens,
+                                void *o, void *workspace, size_t workspace_bytes, int64_t B,
+                                int64_t Hq, int64_t Hkv, int64_t Sq, int64_t D,
+                                int64_t block_size, int64_t max_blocks, int64_t num_blocks,
+                                const int64_t *sq, const int64_t *skc, const int64_t *svc,
+                                const int64_t *sbt, const int64_t *so, float sm_scale,
+                                int causal, int dtype, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -60,6 +60,24 @@ SIGNATURES = {
     "tllm_ipc_open": (ctypes.c_int, [_vp, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p),
                                      ctypes.POINTER(ctypes.c_void_p)]),
     "tllm_ipc_close": (ctypes.c_int, [_vp]),
+    "tllm_paged_kv_append": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+         _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, ctypes.c_int, _vp],
+    ),
+    "tllm_paged_kv_append_rope": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
+         _i64, _i64, _i64, _i64, _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, ctypes.c_float,
+         ctypes.c_int, _vp],
+    ),
+    "tllm_paged_prefill_workspace_size": (ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64, _i64, _i64]),
+    "tllm_paged_prefill": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _i64, _i64, _i64, _i64, _i64, _i64,
+         _i64, _i64, _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, ctypes.c_float, ctypes.c_int,
+         ctypes.c_int, _vp],
+    ),
     "tllm_swiglu": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_int, _vp],

@@ -89,13 +89,15 @@ int encode_tiled(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t rank, voi
 int flash_read_status(int *out);
 int swiglu_read_status(int *out);
 int selftest_read_status(int *out);
+int pkv_read_status(int *out);
+int ppf_read_status(int *out);
 namespace paged {
 int read_status(int *out);
 }
 
 int read_and_clear_device_status(int *out) {
   int (*readers[])(int *) = {flash_read_status, swiglu_read_status, paged::read_status,
-                             selftest_read_status};
+                             selftest_read_status, pkv_read_status, ppf_read_status};
   int first = 0;
   for (auto rd : readers) {
     int v = 0;

@@ -9,14 +9,15 @@
 // second half; the sum of squares is reduced with warp shuffles inside that thread group and
 // the rotate-half pairing (i, i + D/2) never leaves the thread's registers.
 //
-// Numerics follow the oracle: variance and scaling in fp32, the normalised value
-// x * rstd * w rounded to the I/O dtype (norm_rope.py:15), then RoPE in fp32 with one
-// rounding per product (norm_rope.py:28-29), stored in the I/O dtype.
+// Numerics (rmsnorm_rope.cuh) follow the oracle: variance and scaling in fp32, the
+// normalised value x * rstd * w rounded to the I/O dtype (norm_rope.py:15), then RoPE in
+// fp32 with one rounding per product (norm_rope.py:28-29), stored in the I/O dtype.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include "common.h"
 #include "ptx.cuh"
+#include "rmsnorm_rope.cuh"
 
 namespace tllm {
 namespace {
@@ -28,67 +29,7 @@ struct RowGeom {
   int64_t scs, scd, sss, ssd, sw;
 };
 
-template <typename T>
-__device__ __forceinline__ void load8(const T *p, float (&v)[8]) {
-  const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(p));
-  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float2 f = Pack2<T>::unpack(w[i]);
-    v[2 * i] = f.x;
-    v[2 * i + 1] = f.y;
-  }
-}
-
-template <typename T>
-__device__ __forceinline__ void unpack8(const uint4 &raw, float (&v)[8]) {
-  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float2 f = Pack2<T>::unpack(w[i]);
-    v[2 * i] = f.x;
-    v[2 * i + 1] = f.y;
-  }
-}
-
-template <typename T>
-__device__ __forceinline__ void store8(T *p, const float (&v)[8]) {
-  uint4 raw;
-  raw.x = Pack2<T>::pack(v[0], v[1]);
-  raw.y = Pack2<T>::pack(v[2], v[3]);
-  raw.z = Pack2<T>::pack(v[4], v[5]);
-  raw.w = Pack2<T>::pack(v[6], v[7]);
-  *reinterpret_cast<uint4 *>(p) = raw;
-}
-
-template <typename T>
-__device__ __forceinline__ float round_io(float v) {
-  return to_f32<T>(from_f32<T>(v));
-}
-
-// Streaming global accesses: x is read once (no L1 allocation), out is written once.
-__device__ __forceinline__ uint4 ld_stream(const void *p) {
-  uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
-  return r;
-}
-__device__ __forceinline__ void st_stream(void *p, const uint4 &v) {
-  asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y),
-               "r"(v.z), "r"(v.w)
-               : "memory");
-}
-
-template <typename T>
-__device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
-  uint4 raw;
-  raw.x = Pack2<T>::pack(v[0], v[1]);
-  raw.y = Pack2<T>::pack(v[2], v[3]);
-  raw.z = Pack2<T>::pack(v[4], v[5]);
-  raw.w = Pack2<T>::pack(v[6], v[7]);
-  return raw;
-}
+using namespace rr;
 
 // Vector path: unit inner strides, 16-byte aligned rows. A group of TPR = D / 16 threads
 // handles R consecutive heads of one (b, s) position: each thread owns one 16-byte vector
@@ -130,26 +71,11 @@ __global__ void __launch_bounds__(256, 2) rmsnorm_rope_vec_kernel(
   T *orow = out + b * g.sob + s * g.sos + h0 * g.soh;
 #pragma unroll
   for (int u = 0; u < R; ++u) {
-    float x1[8], x2[8];
-    unpack8<T>(x1r[u], x1);
-    unpack8<T>(x2r[u], x2);
-    float ss2 = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) ss2 = fmaf(x1[i], x1[i], fmaf(x2[i], x2[i], ss2));
-#pragma unroll
-    for (int off = TPR / 2; off > 0; off >>= 1) ss2 += __shfl_xor_sync(0xffffffffu, ss2, off);
-    const float rstd = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss2, static_cast<float>(D)), eps));
-    float o1[8], o2[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float y1 = round_io<T>(__fmul_rn(__fmul_rn(x1[i], rstd), w1[i]));
-      const float y2 = round_io<T>(__fmul_rn(__fmul_rn(x2[i], rstd), w2[i]));
-      o1[i] = __fsub_rn(__fmul_rn(y1, c1[i]), __fmul_rn(y2, s1[i]));
-      o2[i] = __fadd_rn(__fmul_rn(y2, c2[i]), __fmul_rn(y1, s2[i]));
-    }
+    uint4 o1, o2;
+    norm_rope_vec<T, D>(x1r[u], x2r[u], w1, w2, c1, c2, s1, s2, eps, o1, o2);
     if (valid) {
-      st_stream(orow + u * g.soh + c, pack8<T>(o1));
-      st_stream(orow + u * g.soh + HALF + c, pack8<T>(o2));
+      st_stream(orow + u * g.soh + c, o1);
+      st_stream(orow + u * g.soh + HALF + c, o2);
     }
   }
 }
