@@ -12,7 +12,8 @@
 // The query rows of a tile are G' heads x S' tokens of one KV head, so every K/V tile loaded
 // serves all of them (G * Sq rows per byte of K/V instead of one). K and V blocks are fetched
 // by TMA straight from the paged pool (one 4-D box of block_size tokens of one head per cache
-// block, coordinates from the block table), 128 tokens per tile, through two-stage rings.
+// block, coordinates from the block table staged in shared memory a window at a time), 128
+// tokens per tile, through rings as deep as shared memory allows (3 stages at D = 128).
 //   warp 0      TMA producer (Q tile once, K/V blocks through the block table)
 //   warp 1      TMEM allocation and the single UMMA-issuing lane: S_j = Q K_j^T into one of
 //               two TMEM S buffers (the next tile's Q K^T overlaps this tile's softmax),
@@ -59,6 +60,7 @@ constexpr int TMEM_COLS = 512;
 constexpr int O_COL = 256;  // S buffers at columns [0,128) and [128,256)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLazyRescaleLog2 = 8.0f;
+constexpr int kBtWin = 256;  // block-table entries staged in shared memory at a time
 
 enum : int {
   SITE_Q = 0x21,
@@ -78,11 +80,18 @@ struct Geo {
   static constexpr int CHUNK_BYTES = BM * SWB;
   static constexpr int TILE_BYTES = BM * D * 2;
   static constexpr uint32_t LAYOUT = SWB == 128 ? 2u : (SWB == 64 ? 4u : 6u);
+  // K/V ring depth: as many stages as 227 KB of shared memory holds (at most 4).
+  static constexpr int kSmemMax = 227 * 1024;
+  static constexpr int kFixed = 256 + 4 * kBtWin + 1024;  // barriers, block-table window, align
+  static constexpr int NST_FIT = (kSmemMax - kFixed - TILE_BYTES) / (2 * TILE_BYTES);
+  static constexpr int NST = NST_FIT > 4 ? 4 : NST_FIT;
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + TILE_BYTES;
-  static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;
-  static constexpr int BAR_OFF = V_OFF + 2 * TILE_BYTES;
-  static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+  static constexpr int V_OFF = K_OFF + NST * TILE_BYTES;
+  static constexpr int BAR_OFF = V_OFF + NST * TILE_BYTES;
+  static constexpr int BT_OFF = BAR_OFF + 256;
+  static constexpr int SMEM_BYTES = BT_OFF + 4 * kBtWin + 1024;
+  static_assert(NST >= 2 && SMEM_BYTES <= kSmemMax, "shared memory plan");
 };
 
 struct Args {
@@ -136,15 +145,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + G::BAR_OFF);
+  constexpr int NST = G::NST;
   uint64_t *q_full = bars + 0;
-  uint64_t *k_full = bars + 1;   // [2]
-  uint64_t *k_empty = bars + 3;  // [2]
-  uint64_t *v_full = bars + 5;   // [2]
-  uint64_t *v_empty = bars + 7;  // [2]
-  uint64_t *s_full = bars + 9;   // [2] per S buffer
-  uint64_t *p_full = bars + 11;
-  uint64_t *pv_done = bars + 12;
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 13);
+  uint64_t *k_full = bars + 1;    // [NST]
+  uint64_t *k_empty = bars + 5;   // [NST]
+  uint64_t *v_full = bars + 9;    // [NST]
+  uint64_t *v_empty = bars + 13;  // [NST]
+  uint64_t *s_full = bars + 17;   // [2] per S buffer
+  uint64_t *p_full = bars + 19;
+  uint64_t *pv_done = bars + 20;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 21);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -172,13 +182,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(q_full), 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(smem_u32(&k_full[s]), 1);
       mbar_init(smem_u32(&k_empty[s]), 1);
       mbar_init(smem_u32(&v_full[s]), 1);
       mbar_init(smem_u32(&v_empty[s]), 1);
-      mbar_init(smem_u32(&s_full[s]), 1);
     }
+    for (int s = 0; s < 2; ++s) mbar_init(smem_u32(&s_full[s]), 1);
     mbar_init(smem_u32(p_full), kSoftmaxThreads);
     mbar_init(smem_u32(pv_done), 1);
     *abort_flag = 0;
@@ -201,52 +211,90 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
-    if (lane == 0 && n > 0) {
-      const uint32_t qb = smem_u32(q_full);
-      mbar_arrive_expect_tx(qb, a.st * a.gt * G::SWB * G::CHUNKS);
+    if (n > 0) {
+      if (lane == 0) {
+        const uint32_t qb = smem_u32(q_full);
+        mbar_arrive_expect_tx(qb, a.st * a.gt * G::SWB * G::CHUNKS);
 #pragma unroll
-      for (int c = 0; c < G::CHUNKS; ++c)
-        tma_load_4d(sQ + c * G::CHUNK_BYTES, &tm_q, qb, c * (G::SWB / 2), s0,
-                    kvh * a.G + g0, b);
+        for (int c = 0; c < G::CHUNKS; ++c)
+          tma_load_4d(sQ + c * G::CHUNK_BYTES, &tm_q, qb, c * (G::SWB / 2), s0,
+                      kvh * a.G + g0, b);
+      }
+      // Block-table entries are staged in shared memory a window at a time by the whole warp
+      // (one round trip per window instead of one per tile); lane 0 issues the TMA loads. K of
+      // tile j goes out one iteration before V of tile j, so waiting for a V slot (which
+      // frees after P V) never holds back the next K tile.
       const int32_t *bt = a.block_tables + b * a.sbt0;
+      int *bt_s = reinterpret_cast<int *>(smem + G::BT_OFF);
       const int bpt = BN / a.block_size;  // cache blocks per key tile
+      const int win_tiles = kBtWin / bpt;
       const int blk_bytes = a.block_size * G::SWB;
-      for (int j = 0; j < n; ++j) {
-        const int s = j & 1;
-        const uint32_t par = ((j >> 1) & 1) ^ 1;
-        const int key0 = (t_begin + j) * BN;
-        const int keys = min(BN, n_keys - key0);
-        const int nblk = (keys + a.block_size - 1) / a.block_size;
+      const int nblk_all = (n_keys + a.block_size - 1) / a.block_size;
+      int phys_prev[8];
+      int nblk_prev = 0;
+      bool ok = true;
+      for (int j = 0; j <= n; ++j) {
         int phys[8];
+        int nblk = 0;
+        if (j < n) {
+          if (j % win_tiles == 0) {
+            const int e0 = (t_begin + j) * bpt;
+            __syncwarp();
+            for (int e = lane; e < kBtWin; e += 32) {
+              int p = a.num_blocks;  // past the pool: TMA fills zeros
+              if (e0 + e < nblk_all) {
+                p = __ldg(bt + static_cast<int64_t>(e0 + e) * a.sbt1);
+                if (p < 0 || p >= a.num_blocks) {
+                  atomicCAS(&g_ppf_status, 0, TLLM_DEV_BAD_INDEX);
+                  p = a.num_blocks;
+                }
+              }
+              bt_s[e] = p;
+            }
+            __syncwarp();
+          }
+          nblk = min(bpt, nblk_all - (t_begin + j) * bpt);
+          const int base = (j % win_tiles) * bpt;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          phys[i] = a.num_blocks;  // past the pool: TMA fills zeros
-          if (i < nblk) {
-            const int p = __ldg(bt + static_cast<int64_t>(key0 / a.block_size + i) * a.sbt1);
-            if (p >= 0 && p < a.num_blocks) phys[i] = p;
-            else atomicCAS(&g_ppf_status, 0, TLLM_DEV_BAD_INDEX);
+          for (int i = 0; i < 8; ++i) phys[i] = i < nblk ? bt_s[base + i] : a.num_blocks;
+        }
+        if (lane == 0 && ok) {
+          if (j < n) {
+            const int st = j % NST;
+            if (!mbar_wait(smem_u32(&k_empty[st]), ((j / NST) & 1) ^ 1, abort_flag, &g_ppf_status,
+                           TLLM_DEV_WAIT_TIMEOUT + SITE_KEMPTY)) {
+              ok = false;
+            } else {
+              const uint32_t kb = smem_u32(&k_full[st]);
+              mbar_arrive_expect_tx(kb, nblk * blk_bytes * G::CHUNKS);
+              for (int i = 0; i < nblk; ++i)
+#pragma unroll
+                for (int c = 0; c < G::CHUNKS; ++c)
+                  tma_load_4d(sK + st * G::TILE_BYTES + c * G::CHUNK_BYTES + i * blk_bytes, &tm_k,
+                              kb, c * (G::SWB / 2), kvh, 0, phys[i]);
+            }
+          }
+          if (ok && j >= 1) {
+            const int jv = j - 1;
+            const int st = jv % NST;
+            if (!mbar_wait(smem_u32(&v_empty[st]), ((jv / NST) & 1) ^ 1, abort_flag,
+                           &g_ppf_status, TLLM_DEV_WAIT_TIMEOUT + SITE_VEMPTY)) {
+              ok = false;
+            } else {
+              const uint32_t vb = smem_u32(&v_full[st]);
+              mbar_arrive_expect_tx(vb, nblk_prev * blk_bytes * G::CHUNKS);
+              for (int i = 0; i < nblk_prev; ++i)
+#pragma unroll
+                for (int c = 0; c < G::CHUNKS; ++c)
+                  tma_load_4d(sV + st * G::TILE_BYTES + c * G::CHUNK_BYTES + i * blk_bytes,
+                              &tm_v, vb, c * (G::SWB / 2), kvh, 0, phys_prev[i]);
+            }
           }
         }
-        if (!mbar_wait(smem_u32(&k_empty[s]), par, abort_flag, &g_ppf_status,
-                       TLLM_DEV_WAIT_TIMEOUT + SITE_KEMPTY))
-          break;
-        const uint32_t kb = smem_u32(&k_full[s]);
-        mbar_arrive_expect_tx(kb, nblk * blk_bytes * G::CHUNKS);
-        for (int i = 0; i < nblk && i < bpt; ++i)
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
 #pragma unroll
-          for (int c = 0; c < G::CHUNKS; ++c)
-            tma_load_4d(sK + s * G::TILE_BYTES + c * G::CHUNK_BYTES + i * blk_bytes, &tm_k, kb,
-                        c * (G::SWB / 2), kvh, 0, phys[i]);
-        if (!mbar_wait(smem_u32(&v_empty[s]), par, abort_flag, &g_ppf_status,
-                       TLLM_DEV_WAIT_TIMEOUT + SITE_VEMPTY))
-          break;
-        const uint32_t vb = smem_u32(&v_full[s]);
-        mbar_arrive_expect_tx(vb, nblk * blk_bytes * G::CHUNKS);
-        for (int i = 0; i < nblk && i < bpt; ++i)
-#pragma unroll
-          for (int c = 0; c < G::CHUNKS; ++c)
-            tma_load_4d(sV + s * G::TILE_BYTES + c * G::CHUNK_BYTES + i * blk_bytes, &tm_v, vb,
-                        c * (G::SWB / 2), kvh, 0, phys[i]);
+        for (int i = 0; i < 8; ++i) phys_prev[i] = phys[i];
+        nblk_prev = nblk;
       }
     }
   } else if (warp == 1) {
@@ -255,13 +303,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc_qk = make_idesc_f16(BM, BN, kBF16, false, false);
       const uint32_t idesc_pv = make_idesc_f16(BM, D, kBF16, false, true);
       auto issue_qk = [&](int j) {
-        const uint32_t kbase = sK + (j & 1) * G::TILE_BYTES;
+        const uint32_t kbase = sK + (j % NST) * G::TILE_BYTES;
 #pragma unroll
         for (int k = 0; k < D / 16; ++k)
           umma_f16_ss(tmem_base + (j & 1) * BN, kmajor_desc<D>(sQ, k), kmajor_desc<D>(kbase, k),
                       idesc_qk, k != 0 ? 1u : 0u);
         umma_commit(smem_u32(&s_full[j & 1]));
-        umma_commit(smem_u32(&k_empty[j & 1]));
+        umma_commit(smem_u32(&k_empty[j % NST]));
       };
       bool ok = mbar_wait(smem_u32(q_full), 0, abort_flag, &g_ppf_status,
                           TLLM_DEV_WAIT_TIMEOUT + SITE_Q);
@@ -274,15 +322,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       for (int j = 0; j < n && ok; ++j) {
-        const int s = j & 1;
+        const int s = j % NST;
         if (!mbar_wait(smem_u32(p_full), j & 1, abort_flag, &g_ppf_status,
                        TLLM_DEV_WAIT_TIMEOUT + SITE_PFULL) ||
-            !mbar_wait(smem_u32(&v_full[s]), (j >> 1) & 1, abort_flag, &g_ppf_status,
+            !mbar_wait(smem_u32(&v_full[s]), (j / NST) & 1, abort_flag, &g_ppf_status,
                        TLLM_DEV_WAIT_TIMEOUT + SITE_VFULL))
           break;
         tc_fence_after();
         const uint32_t vbase = sV + s * G::TILE_BYTES;
-        const uint32_t p_tmem = tmem_base + s * BN;
+        const uint32_t p_tmem = tmem_base + (j & 1) * BN;
 #pragma unroll
         for (int k = 0; k < BN / 16; ++k) {
           const uint64_t bdesc =
@@ -293,8 +341,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(smem_u32(pv_done));
         if (j + 2 < n) {
           // S_j's buffer is rewritten only after the P V above (same tensor pipe, in order).
-          if (!mbar_wait(smem_u32(&k_full[s]), ((j + 2) >> 1) & 1, abort_flag, &g_ppf_status,
-                         TLLM_DEV_WAIT_TIMEOUT + SITE_KFULL))
+          if (!mbar_wait(smem_u32(&k_full[(j + 2) % NST]), ((j + 2) / NST) & 1, abort_flag,
+                         &g_ppf_status, TLLM_DEV_WAIT_TIMEOUT + SITE_KFULL))
             break;
           tc_fence_after();
           issue_qk(j + 2);
@@ -397,13 +445,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (j == n - 1 && tail < BN) {
         // Rows of the last V tile past the item's last key are not real tokens: zero them
         // (thread `row` owns V row `row`) before P V reads the tile.
-        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&v_full[sb]), (j >> 1) & 1, abort_flag,
+        const int vs = j % NST;
+        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&v_full[vs]), (j / NST) & 1, abort_flag,
                                                &g_ppf_status, TLLM_DEV_WAIT_TIMEOUT + SITE_VFULL))) {
           ok = false;
           break;
         }
         if (row >= tail) {
-          uint8_t *vrow = smem + G::V_OFF + sb * G::TILE_BYTES + row * G::SWB;
+          uint8_t *vrow = smem + G::V_OFF + vs * G::TILE_BYTES + row * G::SWB;
 #pragma unroll
           for (int c = 0; c < G::CHUNKS; ++c)
 #pragma unroll
