@@ -60,7 +60,7 @@ constexpr int TMEM_COLS = 512;
 constexpr int O_COL = 256;  // S buffers at columns [0,128) and [128,256)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLazyRescaleLog2 = 8.0f;
-constexpr int kBtWin = 256;  // block-table entries staged in shared memory at a time
+constexpr int kBtWin = 128;  // block-table entries per staged window (two windows)
 
 enum : int {
   SITE_Q = 0x21,
@@ -82,7 +82,7 @@ struct Geo {
   static constexpr uint32_t LAYOUT = SWB == 128 ? 2u : (SWB == 64 ? 4u : 6u);
   // K/V ring depth: as many stages as 227 KB of shared memory holds (at most 4).
   static constexpr int kSmemMax = 227 * 1024;
-  static constexpr int kFixed = 256 + 4 * kBtWin + 1024;  // barriers, block-table window, align
+  static constexpr int kFixed = 256 + 8 * kBtWin + 1024;  // barriers, block-table windows, align
   static constexpr int NST_FIT = (kSmemMax - kFixed - TILE_BYTES) / (2 * TILE_BYTES);
   static constexpr int NST = NST_FIT > 4 ? 4 : NST_FIT;
   static constexpr int Q_OFF = 0;
@@ -90,7 +90,7 @@ struct Geo {
   static constexpr int V_OFF = K_OFF + NST * TILE_BYTES;
   static constexpr int BAR_OFF = V_OFF + NST * TILE_BYTES;
   static constexpr int BT_OFF = BAR_OFF + 256;
-  static constexpr int SMEM_BYTES = BT_OFF + 4 * kBtWin + 1024;
+  static constexpr int SMEM_BYTES = BT_OFF + 8 * kBtWin + 1024;
   static_assert(NST >= 2 && SMEM_BYTES <= kSmemMax, "shared memory plan");
 };
 
@@ -221,80 +221,58 @@ __global__ void __launch_bounds__(kThreads, 1)
                       kvh * a.G + g0, b);
       }
       // Block-table entries are staged in shared memory a window at a time by the whole warp
-      // (one round trip per window instead of one per tile); lane 0 issues the TMA loads. K of
-      // tile j goes out one iteration before V of tile j, so waiting for a V slot (which
+      // (one round trip per window instead of one per tile), in two alternating windows. The
+      // copies of a tile are issued by one lane per (cache block, 128-byte chunk), in one
+      // warp instruction: a single lane issuing them one after another is the bottleneck.
+      // K of tile j goes out one iteration before V of tile j, so waiting for a V slot (which
       // frees after P V) never holds back the next K tile.
       const int32_t *bt = a.block_tables + b * a.sbt0;
-      int *bt_s = reinterpret_cast<int *>(smem + G::BT_OFF);
+      int *bt_s = reinterpret_cast<int *>(smem + G::BT_OFF);  // [2][kBtWin]
       const int bpt = BN / a.block_size;  // cache blocks per key tile
       const int win_tiles = kBtWin / bpt;
       const int blk_bytes = a.block_size * G::SWB;
       const int nblk_all = (n_keys + a.block_size - 1) / a.block_size;
-      int phys_prev[8];
-      int nblk_prev = 0;
-      bool ok = true;
+      const int my_i = lane / G::CHUNKS;  // block of the tile this lane copies
+      const int my_c = lane % G::CHUNKS;  // 128-byte chunk of the row this lane copies
+      // One tile's copies into stage `st` of ring `dst`, completing on `full`.
+      auto issue_tile = [&](int j, uint32_t dst, const CUtensorMap *map, uint64_t *full,
+                            uint64_t *empty) -> bool {
+        const int st = j % NST;
+        const int nblk = min(bpt, nblk_all - (t_begin + j) * bpt);
+        bool got = true;
+        if (lane == 0) {
+          got = mbar_wait(smem_u32(&empty[st]), ((j / NST) & 1) ^ 1, abort_flag, &g_ppf_status,
+                          TLLM_DEV_WAIT_TIMEOUT + (map == &tm_k ? SITE_KEMPTY : SITE_VEMPTY));
+          if (got) mbar_arrive_expect_tx(smem_u32(&full[st]), nblk * blk_bytes * G::CHUNKS);
+        }
+        if (!__shfl_sync(0xffffffffu, got, 0)) return false;
+        if (my_i < nblk) {
+          const int phys = bt_s[((j / win_tiles) & 1) * kBtWin + (j % win_tiles) * bpt + my_i];
+          tma_load_4d(dst + st * G::TILE_BYTES + my_c * G::CHUNK_BYTES + my_i * blk_bytes, map,
+                      smem_u32(&full[st]), my_c * (G::SWB / 2), kvh, 0, phys);
+        }
+        return true;
+      };
       for (int j = 0; j <= n; ++j) {
-        int phys[8];
-        int nblk = 0;
-        if (j < n) {
-          if (j % win_tiles == 0) {
-            const int e0 = (t_begin + j) * bpt;
-            __syncwarp();
-            for (int e = lane; e < kBtWin; e += 32) {
-              int p = a.num_blocks;  // past the pool: TMA fills zeros
-              if (e0 + e < nblk_all) {
-                p = __ldg(bt + static_cast<int64_t>(e0 + e) * a.sbt1);
-                if (p < 0 || p >= a.num_blocks) {
-                  atomicCAS(&g_ppf_status, 0, TLLM_DEV_BAD_INDEX);
-                  p = a.num_blocks;
-                }
+        if (j < n && j % win_tiles == 0) {
+          int *win = bt_s + ((j / win_tiles) & 1) * kBtWin;
+          const int e0 = (t_begin + j) * bpt;
+          __syncwarp();
+          for (int e = lane; e < kBtWin; e += 32) {
+            int p = a.num_blocks;  // past the pool: TMA fills zeros
+            if (e0 + e < nblk_all) {
+              p = __ldg(bt + static_cast<int64_t>(e0 + e) * a.sbt1);
+              if (p < 0 || p >= a.num_blocks) {
+                atomicCAS(&g_ppf_status, 0, TLLM_DEV_BAD_INDEX);
+                p = a.num_blocks;
               }
-              bt_s[e] = p;
             }
-            __syncwarp();
+            win[e] = p;
           }
-          nblk = min(bpt, nblk_all - (t_begin + j) * bpt);
-          const int base = (j % win_tiles) * bpt;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) phys[i] = i < nblk ? bt_s[base + i] : a.num_blocks;
+          __syncwarp();
         }
-        if (lane == 0 && ok) {
-          if (j < n) {
-            const int st = j % NST;
-            if (!mbar_wait(smem_u32(&k_empty[st]), ((j / NST) & 1) ^ 1, abort_flag, &g_ppf_status,
-                           TLLM_DEV_WAIT_TIMEOUT + SITE_KEMPTY)) {
-              ok = false;
-            } else {
-              const uint32_t kb = smem_u32(&k_full[st]);
-              mbar_arrive_expect_tx(kb, nblk * blk_bytes * G::CHUNKS);
-              for (int i = 0; i < nblk; ++i)
-#pragma unroll
-                for (int c = 0; c < G::CHUNKS; ++c)
-                  tma_load_4d(sK + st * G::TILE_BYTES + c * G::CHUNK_BYTES + i * blk_bytes, &tm_k,
-                              kb, c * (G::SWB / 2), kvh, 0, phys[i]);
-            }
-          }
-          if (ok && j >= 1) {
-            const int jv = j - 1;
-            const int st = jv % NST;
-            if (!mbar_wait(smem_u32(&v_empty[st]), ((jv / NST) & 1) ^ 1, abort_flag,
-                           &g_ppf_status, TLLM_DEV_WAIT_TIMEOUT + SITE_VEMPTY)) {
-              ok = false;
-            } else {
-              const uint32_t vb = smem_u32(&v_full[st]);
-              mbar_arrive_expect_tx(vb, nblk_prev * blk_bytes * G::CHUNKS);
-              for (int i = 0; i < nblk_prev; ++i)
-#pragma unroll
-                for (int c = 0; c < G::CHUNKS; ++c)
-                  tma_load_4d(sV + st * G::TILE_BYTES + c * G::CHUNK_BYTES + i * blk_bytes,
-                              &tm_v, vb, c * (G::SWB / 2), kvh, 0, phys_prev[i]);
-            }
-          }
-        }
-        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) phys_prev[i] = phys[i];
-        nblk_prev = nblk;
+        if (j < n && !issue_tile(j, sK, &tm_k, k_full, k_empty)) break;
+        if (j >= 1 && !issue_tile(j - 1, sV, &tm_v, v_full, v_empty)) break;
       }
     }
   } else if (warp == 1) {
