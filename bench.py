@@ -220,6 +220,10 @@ OP_CASES = {
     "paged_small": "paged_attention decode B16 H32 D128 bs16 lens U[512,8192] fp16",
     "rmsnorm": "rmsnorm_rope [2,128,8,64] fp16",
     "rmsnorm_bw": "rmsnorm_rope [16,4096,32,128] fp16",
+    "gqa_decode": "paged_attention_prefill GQA decode B64 Hq32 Hkv8 Sq1 D128 bs16 lens U[512,8192] fp16",
+    "gqa_spec4": "paged_attention_prefill GQA 4-token decode B64 Hq32 Hkv8 Sq4 D128 bs16 lens U[512,8192] fp16",
+    "gqa_chunk": "paged_attention_prefill causal chunk B8 Hq32 Hkv8 Sq512 ctx4096 D128 bs16 fp16",
+    "kv_append_rope": "paged_kv_append_rope B16 T2048 H8 D128 bs16 fp16",
 }
 
 
@@ -240,6 +244,50 @@ def _paged_inputs(torch, batch, seed=3):
     q = torch.randn((batch, 32, 1, 128), generator=gd, device="cuda").half()
     nbytes = int(lens.sum()) * 32 * 128 * 2 * 2 + 2 * batch * 32 * 128 * 2 + sum(nb) * 4 + batch * 4
     return q, kc, vc, bt.cuda(), lens.cuda(), nbytes
+
+
+def _gqa_inputs(torch, batch, hq, hkv, sq, lens=None, seed=3):
+    """Paged GQA case: lens U[512,8192] (seed 3, as the decode case) unless given."""
+    g = torch.Generator().manual_seed(seed)
+    if lens is None:
+        lens = torch.randint(512, 8193, (batch,), dtype=torch.int32, generator=g)
+    nb = [(int(n) + 15) // 16 for n in lens]
+    pool = sum(nb)
+    perm = torch.randperm(pool, generator=g)
+    bt = torch.zeros(batch, max(nb), dtype=torch.int32)
+    pos = 0
+    for i, n in enumerate(nb):
+        bt[i, :n] = perm[pos:pos + n].to(torch.int32)
+        pos += n
+    gd = torch.Generator(device="cuda").manual_seed(seed)
+    kc = torch.randn((pool, 16, hkv, 128), generator=gd, device="cuda").half()
+    vc = torch.randn((pool, 16, hkv, 128), generator=gd, device="cuda").half()
+    q = torch.randn((batch, hq, sq, 128), generator=gd, device="cuda").half()
+    kv_bytes = int(lens.sum()) * hkv * 128 * 2 * 2
+    nbytes = kv_bytes + 2 * batch * hq * sq * 128 * 2 + sum(nb) * 4 + batch * 4
+    # causal FLOPs: query s of a sequence of length n sees n - sq + s + 1 keys
+    keys = sum(sq * int(n) - sq * (sq - 1) // 2 for n in lens)
+    flops = 4.0 * hq * 128 * keys
+    return q, kc, vc, bt.cuda(), lens.cuda(), nbytes, flops
+
+
+def _append_inputs(torch, b=16, t=2048, h=8, d=128, seed=5):
+    gd = torch.Generator(device="cuda").manual_seed(seed)
+    kn = torch.randn((b, t, h, d), generator=gd, device="cuda").half()
+    vn = torch.randn((b, t, h, d), generator=gd, device="cuda").half()
+    nblk = (t + 15) // 16
+    pool = b * nblk
+    perm = torch.randperm(pool, generator=torch.Generator().manual_seed(seed))
+    bt = perm.to(torch.int32).view(b, nblk).cuda()
+    kc = torch.empty((pool, 16, h, d), device="cuda", dtype=torch.float16)
+    vc = torch.empty_like(kc)
+    start = torch.zeros(b, dtype=torch.int32, device="cuda")
+    w = (1 + 0.1 * torch.randn(d, generator=gd, device="cuda")).half()
+    pos = torch.arange(t, device="cuda", dtype=torch.float32)
+    inv = 1.0 / (10000 ** (torch.arange(0, d, 2, device="cuda").float() / d))
+    emb = torch.cat([torch.outer(pos, inv)] * 2, dim=-1)
+    nbytes = 4 * b * t * h * d * 2 + d * 2 + 2 * t * d * 2 + pool * 4 + b * 4
+    return kn, vn, kc, vc, bt, start, w, emb.cos().half(), emb.sin().half(), nbytes
 
 
 def run_op(args):
@@ -268,6 +316,21 @@ def run_op(args):
     elif op in ("paged", "paged_small"):
         q, kc, vc, bt, cl, work = _paged_inputs(torch, 64 if op == "paged" else 16)
         fn, unit = (lambda: T.paged_attention(q, kc, vc, bt, cl, block_size=16)), "GB/s"
+    elif op in ("gqa_decode", "gqa_spec4", "gqa_chunk"):
+        from tritonllmcompiler_b200.ops.paged_kv import paged_attention_prefill
+        if op == "gqa_chunk":
+            q, kc, vc, bt, cl, _, work = _gqa_inputs(
+                torch, 8, 32, 8, 512, lens=torch.full((8,), 4096, dtype=torch.int32))
+            unit = "TFLOP/s"
+        else:
+            q, kc, vc, bt, cl, work, _ = _gqa_inputs(torch, 64, 32, 8, 1 if op == "gqa_decode" else 4)
+            unit = "GB/s"
+        fn = lambda: paged_attention_prefill(q, kc, vc, bt, cl, block_size=16)  # noqa: E731
+    elif op == "kv_append_rope":
+        from tritonllmcompiler_b200.ops.paged_kv import paged_kv_append_rope
+        kn, vn, kc, vc, bt, start, w, cos, sin, work = _append_inputs(torch)
+        fn = lambda: paged_kv_append_rope(kn, vn, w, cos, sin, kc, vc, bt, start, block_size=16)  # noqa: E731
+        unit = "GB/s"
     else:
         b, s, h, d = (2, 128, 8, 64) if op == "rmsnorm" else (16, 4096, 32, 128)
         x = rn((b, s, h, d))
@@ -369,6 +432,43 @@ def extra_ops(torch, T, peaks):
                                               "kv_tokens": int(cl.sum().item()),
                                               "sm_mhz": clk.summary().get("sm_mhz")}
     del kc, vc
+    torch.cuda.empty_cache()
+    # Operators either side of decode (extensions of the reference's set): GQA decode with 1
+    # and 4 new tokens per sequence and a causal prefill chunk through the paged cache, and
+    # the fused K-RoPE cache append.
+    from tritonllmcompiler_b200.ops.paged_kv import paged_attention_prefill, paged_kv_append_rope
+    for name, sq in [("gqa_decode_b64_hq32_hkv8_sq1", 1), ("gqa_decode_b64_hq32_hkv8_sq4", 4)]:
+        q, kc, vc, bt, cl, nbytes, _ = _gqa_inputs(torch, 64, 32, 8, sq)
+        with ClockSampler(torch.cuda.current_device()) as clk:
+            ts = _events_time(torch, lambda: paged_attention_prefill(q, kc, vc, bt, cl, block_size=16),
+                              20, 5, flush)
+        t = statistics.median(ts)
+        gbs = nbytes / (t * 1e-3) / 1e9
+        res[name] = {"value": gbs, "unit": "GB/s", "ms": t, "bytes": nbytes,
+                     "roofline_frac": gbs / hbm, "bound": "hbm", "kv_tokens": int(cl.sum().item()),
+                     "sm_mhz": clk.summary().get("sm_mhz")}
+        del kc, vc
+    q, kc, vc, bt, cl, nbytes, flops = _gqa_inputs(torch, 8, 32, 8, 512,
+                                                   lens=torch.full((8,), 4096, dtype=torch.int32))
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ts = _events_time(torch, lambda: paged_attention_prefill(q, kc, vc, bt, cl, block_size=16),
+                          10, 3, flush)
+    t = statistics.median(ts)
+    tf = flops / (t * 1e-3) / 1e12
+    res["gqa_prefill_chunk_b8_hq32_hkv8_sq512_ctx4096"] = {
+        "value": tf, "unit": "TFLOP/s", "ms": t, "flops": flops, "roofline_frac": tf / tc,
+        "bound": "tensor", "sm_mhz": clk.summary().get("sm_mhz")}
+    del kc, vc
+    kn, vn, kc, vc, bt, start, w, cos, sin, nbytes = _append_inputs(torch)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ts = _events_time(torch, lambda: paged_kv_append_rope(kn, vn, w, cos, sin, kc, vc, bt, start,
+                                                              block_size=16), 20, 5, flush)
+    t = statistics.median(ts)
+    gbs = nbytes / (t * 1e-3) / 1e9
+    res["kv_append_rope_b16_t2048_h8_d128"] = {"value": gbs, "unit": "GB/s", "ms": t, "bytes": nbytes,
+                                               "roofline_frac": gbs / hbm, "bound": "hbm",
+                                               "sm_mhz": clk.summary().get("sm_mhz")}
+    del kn, vn, kc, vc
     torch.cuda.empty_cache()
     return res
 

@@ -60,7 +60,7 @@ struct Geom {
 // Lane groups of TPR = D / 16 lanes; group gi covers heads [R * (gi % (H / R)), ... + R) of
 // token (b, t) = divmod(gi / (H / R), T).
 template <typename T, int D, int R, bool kRope>
-__global__ void __launch_bounds__(256) paged_append_kernel(
+__global__ void __launch_bounds__(256, 2) paged_append_kernel(
     const T *__restrict__ k_new, const T *__restrict__ v_new, T *__restrict__ k_cache,
     T *__restrict__ v_cache, const T *__restrict__ w, const T *__restrict__ cosb,
     const T *__restrict__ sinb, int64_t groups, Geom g) {
