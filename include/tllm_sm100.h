@@ -253,6 +253,24 @@ TLLM_API int tllm_paged_prefill(const void *q, const void *k_cache, const void *
                                 const int64_t *sbt, const int64_t *so, float sm_scale,
                                 int causal, int dtype, void *stream);
 
+/*
+ * Variable-length (packed) flash attention forward. No counterpart in the reference, whose
+ * flash_attention (python/triton_llm/ops/flash_attention.py:107-133) takes padded
+ * [B, H, S, D] tensors: here q/o are [total_q, H, D] and k/v [total_k, Hkv, D] with strides
+ * {row, head, 1} (sq/sk/sv/so hold 3 entries), H % Hkv == 0, and sequence b is rows
+ * [cu_seqlens_q[b], cu_seqlens_q[b+1]) of q/o and [cu_seqlens_k[b], cu_seqlens_k[b+1]) of
+ * k/v (int32 arrays of B + 1 entries on the device). Every sequence is computed as
+ * tllm_flash_attn_fwd would compute it alone (top-left causal mask), query head h reading
+ * key/value head h / (H / Hkv). max_seqlen_q/k must bound every sequence's lengths.
+ */
+TLLM_API int tllm_flash_attn_varlen_fwd(const void *q, const void *k, const void *v, void *o,
+                                        const int *cu_seqlens_q, const int *cu_seqlens_k,
+                                        int64_t B, int64_t H, int64_t Hkv, int64_t total_q,
+                                        int64_t total_k, int64_t max_seqlen_q,
+                                        int64_t max_seqlen_k, int64_t D, const int64_t *sq,
+                                        const int64_t *sk, const int64_t *sv, const int64_t *so,
+                                        float sm_scale, int causal, int dtype, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

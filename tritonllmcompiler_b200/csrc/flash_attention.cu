@@ -94,6 +94,13 @@ struct Args {
   int vec_store;
   int group;    // heads per scheduling group of the two-tile kernel (see pp_item)
   int n_small;  // groups of `group` heads; the rest have group + 1
+  // Packed variable-length sequences (tllm_flash_attn_varlen_fwd): sequence b's query rows
+  // are [cu_q[b], cu_q[b+1]) of q/o, its key rows [cu_k[b], cu_k[b+1]) of k/v; query head h
+  // reads key/value head h / G. Sq and Sk then hold the maximum lengths.
+  const int *cu_q;
+  const int *cu_k;
+  int G;
+  int total_q, total_k;  // rows of q/o and of k/v: cumulative lengths are clamped to them
 };
 
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[32]) { tmem_ld32(taddr, r); }
@@ -441,6 +448,9 @@ struct PPItem {
   int b, h, q0;
   int nkv[2];
   int n_kv;
+  int Sq, Sk;      // this sequence's lengths
+  int qrow, krow;  // first row of the sequence in q/o and in k/v
+  int bc, hk;      // batch coordinate of the tensor maps, key/value head
 };
 
 // Items are numbered in groups of consecutive (b, h) heads: a.n_small groups of a.group
@@ -449,6 +459,7 @@ struct PPItem {
 // Dynamic scheduling in that order ends each group, and the grid, with the lightest items (a
 // short tail), while the CTAs running at the same time read the K/V of only a few heads
 // (they stay in L2).
+template <bool kVarlen>
 __device__ __forceinline__ PPItem pp_item(const Args &a, int item) {
   PPItem w;
   const int n_pairs = (a.n_qtiles + 1) / 2;
@@ -468,12 +479,28 @@ __device__ __forceinline__ PPItem pp_item(const Args &a, int item) {
   w.b = bh / a.H;
   w.h = bh % a.H;
   w.q0 = (n_pairs - 1 - r / heads) * 2 * BM;
-  const int kv_tiles_all = (a.Sk + BN - 1) / BN;
+  if constexpr (kVarlen) {
+    // Clamped to the tensors, so inconsistent offsets cannot move a store out of o.
+    w.qrow = min(max(__ldg(a.cu_q + w.b), 0), a.total_q);
+    w.krow = min(max(__ldg(a.cu_k + w.b), 0), a.total_k);
+    w.Sq = min(max(__ldg(a.cu_q + w.b + 1), w.qrow), a.total_q) - w.qrow;
+    w.Sk = min(max(__ldg(a.cu_k + w.b + 1), w.krow), a.total_k) - w.krow;
+    w.bc = 0;
+    w.hk = w.h / a.G;
+  } else {
+    w.Sq = a.Sq;
+    w.Sk = a.Sk;
+    w.qrow = 0;
+    w.krow = 0;
+    w.bc = w.b;
+    w.hk = w.h;
+  }
+  const int kv_tiles_all = (w.Sk + BN - 1) / BN;
 #pragma unroll
   for (int X = 0; X < 2; ++X) {
     const int qx0 = w.q0 + X * BM;
-    int n = qx0 < a.Sq ? kv_tiles_all : 0;
-    if (a.causal && n > 0) n = min(n, (min(qx0 + BM, a.Sq) - 1) / BN + 1);
+    int n = qx0 < w.Sq ? kv_tiles_all : 0;
+    if (a.causal && n > 0) n = min(n, (min(qx0 + BM, w.Sq) - 1) / BN + 1);
     w.nkv[X] = n;
   }
   w.n_kv = max(w.nkv[0], w.nkv[1]);
@@ -489,7 +516,7 @@ constexpr int kClcReaders = 1 + 8;
 // items still run in launch order, each on the first SM to free up, without a CTA launch and
 // set-up between them; the next item's Q tiles, first key tiles and first S overlap the
 // current item's epilogue.
-template <typename T, int D, bool kSteal>
+template <typename T, int D, bool kSteal, bool kVarlen>
 __global__ void __launch_bounds__(kPPThreads, 1)
     flash_pp_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
@@ -574,7 +601,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       int nq = 0;  // Q loads so far
       bool ok = true;
       for (int it = 0; ok && item >= 0; ++it) {
-        const PPItem w = pp_item(a, item);
+        const PPItem w = pp_item<kVarlen>(a, item);
         if (w.n_kv > 0) {
           // The previous item's last QK has read its Q tiles.
           if (nq > 0 && !mbar_wait(smem_u32(q_empty), (nq - 1) & 1, abort_flag, &g_flash_status,
@@ -588,7 +615,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
 #pragma unroll
             for (int c = 0; c < G::CHUNKS; ++c)
               tma_load_4d(sQ + X * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_q, qb,
-                          c * (G::SWB / 2), w.q0 + X * BM, w.h, w.b);
+                          c * (G::SWB / 2), w.qrow + w.q0 + X * BM, w.h, w.bc);
           }
           ++nq;
           for (int j = 0; j < w.n_kv; ++j, ++g) {
@@ -604,7 +631,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
 #pragma unroll
             for (int c = 0; c < G::CHUNKS; ++c)
               tma_load_4d(sK + s * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_k, kb,
-                          c * (G::SWB / 2), j * BN, w.h, w.b);
+                          c * (G::SWB / 2), w.krow + j * BN, w.hk, w.bc);
             if (!mbar_wait(smem_u32(&v_empty[s]), par, abort_flag, &g_flash_status,
                            TLLM_DEV_WAIT_TIMEOUT + SITE_VEMPTY)) {
               ok = false;
@@ -615,7 +642,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
 #pragma unroll
             for (int c = 0; c < G::CHUNKS; ++c)
               tma_load_4d(sV + s * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_v, vb,
-                          c * (G::SWB / 2), j * BN, w.h, w.b);
+                          c * (G::SWB / 2), w.krow + j * BN, w.hk, w.bc);
           }
         }
         if (!ok || !kSteal) break;
@@ -649,7 +676,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       uint32_t npf[2] = {0u, 0u};  // P tiles consumed per query tile
       bool ok = true;
       for (int it = 0; ok && item >= 0; ++it) {
-        const PPItem w = pp_item(a, item);
+        const PPItem w = pp_item<kVarlen>(a, item);
         if (w.n_kv > 0) {
           ok = mbar_wait(smem_u32(q_full), nq & 1, abort_flag, &g_flash_status,
                          TLLM_DEV_WAIT_TIMEOUT + SITE_Q) &&
@@ -737,7 +764,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     uint32_t nod = 0;  // O tiles finished
     bool ok = true;
     for (int it = 0; ok && item >= 0; ++it) {
-      const PPItem w = pp_item(a, item);
+      const PPItem w = pp_item<kVarlen>(a, item);
       const int qx0 = w.q0 + X * BM;
       const int qg = qx0 + row;
       const int nk = w.nkv[X];
@@ -752,7 +779,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         }
         tc_fence_after();
         const int k0 = j * BN;
-        const bool need_mask = (k0 + BN > a.Sk) || (a.causal && k0 + BN - 1 > qx0);
+        const bool need_mask = (k0 + BN > w.Sk) || (a.causal && k0 + BN - 1 > qx0);
         // The whole S row in one TMEM round trip (four 32-column loads, one wait).
         uint32_t sr[BN];
         tmem_ld4x32(s_tm, sr);
@@ -760,7 +787,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
 #pragma unroll
           for (int t = 0; t < BN; ++t) {
             const int kg = k0 + t;
-            if (kg >= a.Sk || (a.causal && kg > qg)) sr[t] = __float_as_uint(-INFINITY);
+            if (kg >= w.Sk || (a.causal && kg > qg)) sr[t] = __float_as_uint(-INFINITY);
           }
         }
         // Row max on the raw scores (the scale is positive): an 8-way tree of 3-input maxima.
@@ -839,12 +866,12 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         tc_fence_after();
         const float inv_l = 1.0f / l_run;
         T *orow = static_cast<T *>(a.o) + w.b * a.so0 + w.h * a.so1 +
-                  static_cast<int64_t>(qg) * a.so2;
+                  static_cast<int64_t>(w.qrow + qg) * a.so2;
 #pragma unroll 1
         for (int c = 0; c < D; c += OC) {
           uint32_t r[OC];
           tmem_ld_cols(o_tm + c, r);
-          if (qg < a.Sq) {
+          if (qg < w.Sq) {
             if (a.vec_store) {
 #pragma unroll
               for (int t = 0; t < OC; t += 8) {
@@ -864,10 +891,10 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         }
         // The O_X reads above complete (tcgen05.wait::ld) before this warp's next P store,
         // which the next item's first PV_X waits for.
-      } else if (qx0 < a.Sq && qg < a.Sq) {
+      } else if (qx0 < w.Sq && qg < w.Sq) {
         // No keys at all (Sk == 0): 0/0, as in the reference.
         T *orow = static_cast<T *>(a.o) + w.b * a.so0 + w.h * a.so1 +
-                  static_cast<int64_t>(qg) * a.so2;
+                  static_cast<int64_t>(w.qrow + qg) * a.so2;
         for (int c = 0; c < D; ++c) orow[c * a.so3] = from_f32<T>(NAN);
       }
       if (!kSteal) break;
@@ -894,10 +921,19 @@ constexpr int kVariantPingPong = 0;
 constexpr int kVariantSingleTile = 1;
 constexpr int kVariantPingPongOneItem = 2;
 
+// Packed variable-length batch: sequence b's rows are [cu_q[b], cu_q[b+1]) of q/o (total_q
+// rows) and [cu_k[b], cu_k[b+1]) of k/v (total_k rows, Hkv heads).
+struct VarlenDesc {
+  const int *cu_q;
+  const int *cu_k;
+  int64_t total_q, total_k, Hkv;
+};
+
 template <typename T, int D>
 int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, int64_t H,
              int64_t Sq, int64_t Sk, const int64_t *sq, const int64_t *sk, const int64_t *sv,
-             const int64_t *so, float sm_scale, int causal, int variant, cudaStream_t st) {
+             const int64_t *so, float sm_scale, int causal, int variant, cudaStream_t st,
+             const VarlenDesc *vl = nullptr) {
   using G = Geo<D>;
   const CUtensorMapDataType dt = std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                                  : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -905,15 +941,22 @@ int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, in
                                 : (G::SWB == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
   const uint32_t box[4] = {static_cast<uint32_t>(G::SWB / 2), static_cast<uint32_t>(BM), 1, 1};
   CUtensorMap mq, mk, mv;
+  // Dense: 4-D maps {D, S, H, B}. Packed: {D, total rows, H, 1} (the strides arrays then hold
+  // {unused, head, row, 1}).
+  const int64_t q_rows = vl ? vl->total_q : Sq;
+  const int64_t k_rows = vl ? vl->total_k : Sk;
+  const int64_t kv_heads = vl ? vl->Hkv : H;
+  const int64_t map_b = vl ? 1 : B;
   {
-    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)Sq, (uint64_t)H, (uint64_t)B};
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)q_rows, (uint64_t)H, (uint64_t)map_b};
     const uint64_t str[3] = {(uint64_t)sq[2] * 2, (uint64_t)sq[1] * 2, (uint64_t)sq[0] * 2};
     int rc = encode_tiled(&mq, dt, 4, const_cast<void *>(q), dims, str, box, sw);
     if (rc) return rc;
   }
   {
     // Sk == 0 launches no key loads; the map still needs a non-zero extent.
-    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)(Sk > 0 ? Sk : 1), (uint64_t)H, (uint64_t)B};
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)(k_rows > 0 ? k_rows : 1), (uint64_t)kv_heads,
+                              (uint64_t)map_b};
     const uint64_t strk[3] = {(uint64_t)sk[2] * 2, (uint64_t)sk[1] * 2, (uint64_t)sk[0] * 2};
     int rc = encode_tiled(&mk, dt, 4, const_cast<void *>(k), dims, strk, box, sw);
     if (rc) return rc;
@@ -934,6 +977,11 @@ int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, in
   a.scale_log2 = sm_scale * kLog2e;
   a.causal = causal ? 1 : 0;
   a.vec_store = (so[3] == 1 && so[0] % 8 == 0 && so[1] % 8 == 0 && so[2] % 8 == 0 && aligned16(o)) ? 1 : 0;
+  a.cu_q = vl ? vl->cu_q : nullptr;
+  a.cu_k = vl ? vl->cu_k : nullptr;
+  a.G = vl ? static_cast<int>(H / vl->Hkv) : 1;
+  a.total_q = vl ? static_cast<int>(vl->total_q) : 0;
+  a.total_k = vl ? static_cast<int>(vl->total_k) : 0;
   {
     // Scheduling groups of the two-tile kernel: kGroupHeads heads per group, or all heads in
     // one group when a causal grid is only a few waves long (its tail then comes from the
@@ -949,7 +997,7 @@ int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, in
     a.group = static_cast<int>(bh / n_groups);
     a.n_small = static_cast<int>(n_groups - bh % n_groups);
   }
-  if (variant == kVariantSingleTile) {
+  if (variant == kVariantSingleTile && !vl) {
     auto kern = flash_fwd_kernel<T, D>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(flash)");
@@ -958,8 +1006,9 @@ int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, in
     return cuda_status(cudaGetLastError(), "flash launch");
   }
   using GP = GeoPP<D>;
-  auto kern = variant == kVariantPingPongOneItem ? flash_pp_kernel<T, D, false>
-                                                 : flash_pp_kernel<T, D, true>;
+  auto kern = vl ? flash_pp_kernel<T, D, true, true>
+                : (variant == kVariantPingPongOneItem ? flash_pp_kernel<T, D, false, false>
+                                                      : flash_pp_kernel<T, D, true, false>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GP::SMEM_BYTES);
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(flash pp)");
   // setmaxnreg.inc only completes if the launch holds the registers the split assumes.
@@ -982,12 +1031,13 @@ int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, in
 template <typename T>
 int launch(const void *q, const void *k, const void *v, void *o, int64_t B, int64_t H, int64_t Sq,
            int64_t Sk, int64_t D, const int64_t *sq, const int64_t *sk, const int64_t *sv,
-           const int64_t *so, float sm_scale, int causal, int variant, cudaStream_t st) {
+           const int64_t *so, float sm_scale, int causal, int variant, cudaStream_t st,
+           const VarlenDesc *vl = nullptr) {
   switch (D) {
-    case 16: return launch_d<T, 16>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st);
-    case 32: return launch_d<T, 32>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st);
-    case 64: return launch_d<T, 64>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st);
-    default: return launch_d<T, 128>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st);
+    case 16: return launch_d<T, 16>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st, vl);
+    case 32: return launch_d<T, 32>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st, vl);
+    case 64: return launch_d<T, 64>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st, vl);
+    default: return launch_d<T, 128>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st, vl);
   }
 }
 
@@ -1051,4 +1101,59 @@ extern "C" int tllm_flash_attn_fwd_variant(const void *q, const void *k, const v
                                            int causal, int dtype, int variant, void *stream) {
   return tllm::flash::entry(q, k, v, o, B, H, Sq, Sk, D, sq, sk, sv, so, sm_scale, causal, dtype,
                             variant, stream);
+}
+
+// Packed variable-length batch (no counterpart in the reference, whose flash_attention takes
+// padded [B, H, S, D] tensors): q/o [total_q, H, D], k/v [total_k, Hkv, D] with strides
+// {row, head, 1}; sequence b is rows [cu_q[b], cu_q[b+1]) of q/o and [cu_k[b], cu_k[b+1]) of
+// k/v (int32, on the device); the causal mask is top-left aligned per sequence, as in
+// flash_attention.
+extern "C" int tllm_flash_attn_varlen_fwd(const void *q, const void *k, const void *v, void *o,
+                                          const int *cu_seqlens_q, const int *cu_seqlens_k,
+                                          int64_t B, int64_t H, int64_t Hkv, int64_t total_q,
+                                          int64_t total_k, int64_t max_seqlen_q,
+                                          int64_t max_seqlen_k, int64_t D, const int64_t *sq,
+                                          const int64_t *sk, const int64_t *sv, const int64_t *so,
+                                          float sm_scale, int causal, int dtype, void *stream) {
+  using namespace tllm;
+  using namespace tllm::flash;
+  clear_error();
+  TLLM_CHECK_ARG(B >= 0 && H >= 0 && Hkv >= 0 && total_q >= 0 && total_k >= 0 &&
+                     max_seqlen_q >= 0 && max_seqlen_k >= 0,
+                 "flash_attention_varlen: negative dimension");
+  TLLM_CHECK_ARG(D == 16 || D == 32 || D == 64 || D == 128,
+                 "flash_attention_varlen: head dim %lld not in {16,32,64,128}", (long long)D);
+  TLLM_CHECK_ARG(dtype == TLLM_DTYPE_F16 || dtype == TLLM_DTYPE_BF16,
+                 "flash_attention_varlen: unsupported dtype %d", dtype);
+  TLLM_CHECK_ARG(sq && sk && sv && so, "flash_attention_varlen: null stride array");
+  if (B == 0 || H == 0 || max_seqlen_q == 0 || total_q == 0) return TLLM_OK;
+  TLLM_CHECK_ARG(Hkv >= 1 && H % Hkv == 0,
+                 "flash_attention_varlen: %lld query heads do not group over %lld key/value heads",
+                 (long long)H, (long long)Hkv);
+  TLLM_CHECK_ARG(q && k && v && o && cu_seqlens_q && cu_seqlens_k,
+                 "flash_attention_varlen: null pointer");
+  TLLM_CHECK_ARG(total_q < (1LL << 31) && total_k < (1LL << 31) && B * H < (1LL << 31) &&
+                     max_seqlen_q < (1LL << 31) && max_seqlen_k < (1LL << 31),
+                 "flash_attention_varlen: problem too large");
+  TLLM_CHECK_ARG(B * H * ((max_seqlen_q + 255) / 256) < (1LL << 31),
+                 "flash_attention_varlen: grid too large");
+  TLLM_CHECK_ARG(sq[2] == 1 && sk[2] == 1 && sv[2] == 1,
+                 "flash_attention_varlen: q/k/v need a unit innermost stride");
+  for (int i = 0; i < 2; ++i)
+    TLLM_CHECK_ARG(sq[i] % 8 == 0 && sk[i] % 8 == 0 && sv[i] % 8 == 0,
+                   "flash_attention_varlen: q/k/v strides must be multiples of 8 elements");
+  TLLM_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v),
+                 "flash_attention_varlen: q/k/v must be 16-byte aligned");
+  // As the dense launcher's {batch, head, row, 1} stride arrays; the batch stride is unused.
+  const int64_t sq4[4] = {sq[0], sq[1], sq[0], 1};
+  const int64_t sk4[4] = {sk[0], sk[1], sk[0], 1};
+  const int64_t sv4[4] = {sv[0], sv[1], sv[0], 1};
+  const int64_t so4[4] = {0, so[1], so[0], so[2]};
+  const VarlenDesc vl{cu_seqlens_q, cu_seqlens_k, total_q, total_k, Hkv};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == TLLM_DTYPE_F16)
+    return launch<__half>(q, k, v, o, B, H, max_seqlen_q, max_seqlen_k, D, sq4, sk4, sv4, so4,
+                          sm_scale, causal, kVariantPingPong, st, &vl);
+  return launch<__nv_bfloat16>(q, k, v, o, B, H, max_seqlen_q, max_seqlen_k, D, sq4, sk4, sv4,
+                               so4, sm_scale, causal, kVariantPingPong, st, &vl);
 }
