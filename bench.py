@@ -224,6 +224,7 @@ OP_CASES = {
     "gqa_spec4": "paged_attention_prefill GQA 4-token decode B64 Hq32 Hkv8 Sq4 D128 bs16 lens U[512,8192] fp16",
     "gqa_chunk": "paged_attention_prefill causal chunk B8 Hq32 Hkv8 Sq512 ctx4096 D128 bs16 fp16",
     "kv_append_rope": "paged_kv_append_rope B16 T2048 H8 D128 bs16 fp16",
+    "flash_varlen": "flash_attention_varlen causal 16 sequences U[256,4096] H32 D128 fp16",
 }
 
 
@@ -290,6 +291,19 @@ def _append_inputs(torch, b=16, t=2048, h=8, d=128, seed=5):
     return kn, vn, kc, vc, bt, start, w, emb.cos().half(), emb.sin().half(), nbytes
 
 
+def _varlen_inputs(torch, n=16, h=32, d=128, seed=6):
+    """Packed prefill batch: n sequences with lengths U[256, 4096] (seed 6)."""
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(256, 4097, (n,), generator=g)
+    cu = torch.zeros(n + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(lens, 0)
+    total = int(cu[-1])
+    gd = torch.Generator(device="cuda").manual_seed(seed)
+    q, k, v = (torch.randn((total, h, d), generator=gd, device="cuda").half() for _ in range(3))
+    flops = sum(4.0 * h * d * int(x) * int(x) * 0.5 for x in lens)
+    return q, k, v, cu.cuda(), int(lens.max()), flops
+
+
 def run_op(args):
     """Runs one operator case warmup+steps times; prints {"op", "ms", "value", "unit"}."""
     import torch
@@ -326,6 +340,11 @@ def run_op(args):
             q, kc, vc, bt, cl, work, _ = _gqa_inputs(torch, 64, 32, 8, 1 if op == "gqa_decode" else 4)
             unit = "GB/s"
         fn = lambda: paged_attention_prefill(q, kc, vc, bt, cl, block_size=16)  # noqa: E731
+    elif op == "flash_varlen":
+        from tritonllmcompiler_b200.ops.flash_varlen import flash_attention_varlen
+        q, k, v, cu, mx, work = _varlen_inputs(torch)
+        fn = lambda: flash_attention_varlen(q, k, v, cu, cu, mx, mx, causal=True)  # noqa: E731
+        unit = "TFLOP/s"
     elif op == "kv_append_rope":
         from tritonllmcompiler_b200.ops.paged_kv import paged_kv_append_rope
         kn, vn, kc, vc, bt, start, w, cos, sin, work = _append_inputs(torch)
@@ -459,6 +478,17 @@ def extra_ops(torch, T, peaks):
         "value": tf, "unit": "TFLOP/s", "ms": t, "flops": flops, "roofline_frac": tf / tc,
         "bound": "tensor", "sm_mhz": clk.summary().get("sm_mhz")}
     del kc, vc
+    from tritonllmcompiler_b200.ops.flash_varlen import flash_attention_varlen
+    q, k, v, cu, mx, flops = _varlen_inputs(torch)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ts = _events_time(torch, lambda: flash_attention_varlen(q, k, v, cu, cu, mx, mx, causal=True),
+                          10, 3, flush)
+    t = statistics.median(ts)
+    tf = flops / (t * 1e-3) / 1e12
+    res["flash_varlen_causal_16seq_u256_4096_h32_d128"] = {
+        "value": tf, "unit": "TFLOP/s", "ms": t, "flops": flops, "roofline_frac": tf / tc,
+        "bound": "tensor", "sm_mhz": clk.summary().get("sm_mhz")}
+    del q, k, v
     kn, vn, kc, vc, bt, start, w, cos, sin, nbytes = _append_inputs(torch)
     with ClockSampler(torch.cuda.current_device()) as clk:
         ts = _events_time(torch, lambda: paged_kv_append_rope(kn, vn, w, cos, sin, kc, vc, bt, start,
