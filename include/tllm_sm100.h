@@ -271,6 +271,32 @@ TLLM_API int tllm_flash_attn_varlen_fwd(const void *q, const void *k, const void
                                         const int64_t *sk, const int64_t *sv, const int64_t *so,
                                         float sm_scale, int causal, int dtype, void *stream);
 
+/*
+ * FlashAttention backward. No counterpart in the reference, which has the forward only
+ * (python/triton_llm/ops/flash_attention.py:1-7); the function differentiated is its
+ * flash_attention (top-left causal mask). tllm_flash_attn_fwd_lse is tllm_flash_attn_fwd
+ * that also writes lse [B, H, Sq] (fp32, contiguous): log2 of each row's softmax normaliser
+ * in units of s * sm_scale * log2(e). tllm_flash_attn_bwd takes q, k, v, the forward's output
+ * o and lse, and dout (all [B, H, S, D] with the layout rules of tllm_flash_attn_fwd, D 64 or
+ * 128) and writes dq, dk, dv ([B, H, S, D], any strides). The workspace (16-byte aligned,
+ * tllm_flash_attn_bwd_workspace_size bytes) holds the fp32 dq accumulator and the per-row
+ * rowsum(dout * o); the call clears what it uses.
+ */
+TLLM_API int tllm_flash_attn_fwd_lse(const void *q, const void *k, const void *v, void *o,
+                                     float *lse, int64_t B, int64_t H, int64_t Sq, int64_t Sk,
+                                     int64_t D, const int64_t *sq, const int64_t *sk,
+                                     const int64_t *sv, const int64_t *so, float sm_scale,
+                                     int causal, int dtype, void *stream);
+TLLM_API size_t tllm_flash_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t Sq, int64_t D);
+TLLM_API int tllm_flash_attn_bwd(const void *q, const void *k, const void *v, const void *o,
+                                 const void *dout, const float *lse, void *dq, void *dk, void *dv,
+                                 void *workspace, size_t workspace_bytes, int64_t B, int64_t H,
+                                 int64_t Sq, int64_t Sk, int64_t D, const int64_t *sq,
+                                 const int64_t *sk, const int64_t *sv, const int64_t *so,
+                                 const int64_t *sdo, const int64_t *sdq, const int64_t *sdk,
+                                 const int64_t *sdv, float sm_scale, int causal, int dtype,
+                                 void *stream);
+
 #ifdef __cplusplus
 }
 #endif

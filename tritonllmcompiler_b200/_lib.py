@@ -83,6 +83,18 @@ SIGNATURES = {
         [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
          _c_i64p, _c_i64p, _c_i64p, _c_i64p, ctypes.c_float, ctypes.c_int, ctypes.c_int, _vp],
     ),
+    "tllm_flash_attn_fwd_lse": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _c_i64p, _c_i64p, _c_i64p,
+         _c_i64p, ctypes.c_float, ctypes.c_int, ctypes.c_int, _vp],
+    ),
+    "tllm_flash_attn_bwd_workspace_size": (ctypes.c_size_t, [_i64, _i64, _i64, _i64]),
+    "tllm_flash_attn_bwd": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _i64, _i64, _i64,
+         _i64, _i64, _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p,
+         ctypes.c_float, ctypes.c_int, ctypes.c_int, _vp],
+    ),
     "tllm_swiglu": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_int, _vp],

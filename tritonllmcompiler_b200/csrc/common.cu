@@ -73,6 +73,18 @@ int encode_tiled(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t rank, voi
       return cuda_status(g_encode_status, "cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)");
     return fail(TLLM_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   }
+  // The driver call needs the device's context current on this thread; a thread that has
+  // not made a runtime call yet (for example torch's autograd worker) may not have it, and
+  // cudaSetDevice binds the primary context.
+  {
+    thread_local int bound_dev = -1;
+    int dev = -1;
+    if (cudaGetDevice(&dev) == cudaSuccess && dev != bound_dev) {
+      cudaError_t e = cudaSetDevice(dev);
+      if (e != cudaSuccess) return cuda_status(e, "cudaSetDevice");
+      bound_dev = dev;
+    }
+  }
   cuuint32_t elem_strides[5] = {1, 1, 1, 1, 1};
   CUresult r = g_encode(map, dtype, rank, base, reinterpret_cast<const cuuint64_t *>(dims),
                         reinterpret_cast<const cuuint64_t *>(strides_bytes),
@@ -91,13 +103,15 @@ int swiglu_read_status(int *out);
 int selftest_read_status(int *out);
 int pkv_read_status(int *out);
 int ppf_read_status(int *out);
+int fbwd_read_status(int *out);
 namespace paged {
 int read_status(int *out);
 }
 
 int read_and_clear_device_status(int *out) {
   int (*readers[])(int *) = {flash_read_status, swiglu_read_status, paged::read_status,
-                             selftest_read_status, pkv_read_status, ppf_read_status};
+                             selftest_read_status, pkv_read_status, ppf_read_status,
+                             fbwd_read_status};
   int first = 0;
   for (auto rd : readers) {
     int v = 0;

@@ -101,6 +101,10 @@ struct Args {
   const int *cu_k;
   int G;
   int total_q, total_k;  // rows of q/o and of k/v: cumulative lengths are clamped to them
+  // Optional [B, H, Sq] fp32 output (dense batches): log2 of each row's softmax normaliser in
+  // the units of s * scale * log2(e), i.e. P = 2^(s * scale * log2(e) - lse). The backward
+  // pass recomputes P from it.
+  float *lse;
 };
 
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[32]) { tmem_ld32(taddr, r); }
@@ -865,6 +869,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         ++nod;
         tc_fence_after();
         const float inv_l = 1.0f / l_run;
+        if (!kVarlen && a.lse != nullptr && qg < w.Sq)
+          a.lse[(static_cast<int64_t>(w.b) * a.H + w.h) * a.Sq + qg] = m_use + log2f(l_run);
         T *orow = static_cast<T *>(a.o) + w.b * a.so0 + w.h * a.so1 +
                   static_cast<int64_t>(w.qrow + qg) * a.so2;
 #pragma unroll 1
@@ -933,7 +939,7 @@ template <typename T, int D>
 int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, int64_t H,
              int64_t Sq, int64_t Sk, const int64_t *sq, const int64_t *sk, const int64_t *sv,
              const int64_t *so, float sm_scale, int causal, int variant, cudaStream_t st,
-             const VarlenDesc *vl = nullptr) {
+             const VarlenDesc *vl = nullptr, float *lse = nullptr) {
   using G = Geo<D>;
   const CUtensorMapDataType dt = std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                                  : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -977,6 +983,7 @@ int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, in
   a.scale_log2 = sm_scale * kLog2e;
   a.causal = causal ? 1 : 0;
   a.vec_store = (so[3] == 1 && so[0] % 8 == 0 && so[1] % 8 == 0 && so[2] % 8 == 0 && aligned16(o)) ? 1 : 0;
+  a.lse = lse;
   a.cu_q = vl ? vl->cu_q : nullptr;
   a.cu_k = vl ? vl->cu_k : nullptr;
   a.G = vl ? static_cast<int>(H / vl->Hkv) : 1;
@@ -1032,12 +1039,12 @@ template <typename T>
 int launch(const void *q, const void *k, const void *v, void *o, int64_t B, int64_t H, int64_t Sq,
            int64_t Sk, int64_t D, const int64_t *sq, const int64_t *sk, const int64_t *sv,
            const int64_t *so, float sm_scale, int causal, int variant, cudaStream_t st,
-           const VarlenDesc *vl = nullptr) {
+           const VarlenDesc *vl = nullptr, float *lse = nullptr) {
   switch (D) {
-    case 16: return launch_d<T, 16>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st, vl);
-    case 32: return launch_d<T, 32>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st, vl);
-    case 64: return launch_d<T, 64>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st, vl);
-    default: return launch_d<T, 128>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st, vl);
+    case 16: return launch_d<T, 16>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st, vl, lse);
+    case 32: return launch_d<T, 32>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st, vl, lse);
+    case 64: return launch_d<T, 64>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st, vl, lse);
+    default: return launch_d<T, 128>(q, k, v, o, B, H, Sq, Sk, sq, sk, sv, so, sm_scale, causal, variant, st, vl, lse);
   }
 }
 
@@ -1051,7 +1058,8 @@ namespace {
 
 int entry(const void *q, const void *k, const void *v, void *o, int64_t B, int64_t H, int64_t Sq,
           int64_t Sk, int64_t D, const int64_t *sq, const int64_t *sk, const int64_t *sv,
-          const int64_t *so, float sm_scale, int causal, int dtype, int variant, void *stream) {
+          const int64_t *so, float sm_scale, int causal, int dtype, int variant, void *stream,
+          float *lse = nullptr) {
   clear_error();
   TLLM_CHECK_ARG(B >= 0 && H >= 0 && Sq >= 0 && Sk >= 0, "flash_attention: negative dimension");
   TLLM_CHECK_ARG(D == 16 || D == 32 || D == 64 || D == 128,
@@ -1076,9 +1084,10 @@ int entry(const void *q, const void *k, const void *v, void *o, int64_t B, int64
                  "flash_attention: q/k/v must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == TLLM_DTYPE_F16)
-    return launch<__half>(q, k, v, o, B, H, Sq, Sk, D, sq, sk, sv, so, sm_scale, causal, variant, st);
+    return launch<__half>(q, k, v, o, B, H, Sq, Sk, D, sq, sk, sv, so, sm_scale, causal, variant, st,
+                          nullptr, lse);
   return launch<__nv_bfloat16>(q, k, v, o, B, H, Sq, Sk, D, sq, sk, sv, so, sm_scale, causal,
-                               variant, st);
+                               variant, st, nullptr, lse);
 }
 
 }  // namespace
@@ -1101,6 +1110,22 @@ extern "C" int tllm_flash_attn_fwd_variant(const void *q, const void *k, const v
                                            int causal, int dtype, int variant, void *stream) {
   return tllm::flash::entry(q, k, v, o, B, H, Sq, Sk, D, sq, sk, sv, so, sm_scale, causal, dtype,
                             variant, stream);
+}
+
+// tllm_flash_attn_fwd that also writes each query row's softmax log-normaliser (lse, fp32
+// [B, H, Sq] contiguous) for the backward pass; no counterpart in the reference, which has the
+// forward only.
+extern "C" int tllm_flash_attn_fwd_lse(const void *q, const void *k, const void *v, void *o,
+                                       float *lse, int64_t B, int64_t H, int64_t Sq, int64_t Sk,
+                                       int64_t D, const int64_t *sq, const int64_t *sk,
+                                       const int64_t *sv, const int64_t *so, float sm_scale,
+                                       int causal, int dtype, void *stream) {
+  if (!lse && B > 0 && H > 0 && Sq > 0) {
+    tllm::clear_error();
+    return tllm::fail(TLLM_ERR_INVALID, "flash_attention: null lse pointer");
+  }
+  return tllm::flash::entry(q, k, v, o, B, H, Sq, Sk, D, sq, sk, sv, so, sm_scale, causal, dtype,
+                            tllm::flash::kVariantPingPong, stream, lse);
 }
 
 // Packed variable-length batch (no counterpart in the reference, whose flash_attention takes
