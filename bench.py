@@ -225,6 +225,7 @@ OP_CASES = {
     "gqa_chunk": "paged_attention_prefill causal chunk B8 Hq32 Hkv8 Sq512 ctx4096 D128 bs16 fp16",
     "kv_append_rope": "paged_kv_append_rope B16 T2048 H8 D128 bs16 fp16",
     "flash_varlen": "flash_attention_varlen causal 16 sequences U[256,4096] H32 D128 fp16",
+    "flash_bwd": "flash_attention_backward causal [4,32,4096,128] fp16",
 }
 
 
@@ -345,6 +346,12 @@ def run_op(args):
         q, k, v, cu, mx, work = _varlen_inputs(torch)
         fn = lambda: flash_attention_varlen(q, k, v, cu, cu, mx, mx, causal=True)  # noqa: E731
         unit = "TFLOP/s"
+    elif op == "flash_bwd":
+        from tritonllmcompiler_b200.ops.flash_backward import flash_attention_backward, flash_attention_fwd_lse
+        q, k, v, do = rn((4, 32, 4096, 128)), rn((4, 32, 4096, 128)), rn((4, 32, 4096, 128)), rn((4, 32, 4096, 128))
+        o, lse = flash_attention_fwd_lse(q, k, v, causal=True)
+        fn = lambda: flash_attention_backward(q, k, v, o, lse, do, causal=True)  # noqa: E731
+        work, unit = 2.5 * 4.0 * 4 * 32 * 4096 * 4096 * 128 * 0.5, "TFLOP/s"
     elif op == "kv_append_rope":
         from tritonllmcompiler_b200.ops.paged_kv import paged_kv_append_rope
         kn, vn, kc, vc, bt, start, w, cos, sin, work = _append_inputs(torch)
@@ -478,6 +485,21 @@ def extra_ops(torch, T, peaks):
         "value": tf, "unit": "TFLOP/s", "ms": t, "flops": flops, "roofline_frac": tf / tc,
         "bound": "tensor", "sm_mhz": clk.summary().get("sm_mhz")}
     del kc, vc
+    # FlashAttention backward, causal [4,32,4096,128]: 2.5x the forward's FLOPs (five GEMMs
+    # against two), the FlashAttention convention.
+    from tritonllmcompiler_b200.ops.flash_backward import flash_attention_backward, flash_attention_fwd_lse
+    q, k, v, do = (gen((4, 32, 4096, 128), s_) for s_ in (2, 3, 4, 5))
+    o, lse = flash_attention_fwd_lse(q, k, v, causal=True)
+    flops = 2.5 * 4.0 * 4 * 32 * 4096 * 4096 * 128 * 0.5
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ts = _events_time(torch, lambda: flash_attention_backward(q, k, v, o, lse, do, causal=True), 5, 3, flush)
+    t = statistics.median(ts)
+    tf = flops / (t * 1e-3) / 1e12
+    res["flash_bwd_causal_4x32x4096x128"] = {"value": tf, "unit": "TFLOP/s", "ms": t, "flops": flops,
+                                             "roofline_frac": tf / tc, "bound": "tensor",
+                                             "sm_mhz": clk.summary().get("sm_mhz")}
+    del q, k, v, do, o, lse
+    torch.cuda.empty_cache()
     from tritonllmcompiler_b200.ops.flash_varlen import flash_attention_varlen
     q, k, v, cu, mx, flops = _varlen_inputs(torch)
     with ClockSampler(torch.cuda.current_device()) as clk:

@@ -18,8 +18,10 @@
 //                 dQ = dS K_j         -> TMEM [0,D)        (A = dS, K-major)
 //   warps 2-5   one query row per thread: P = 2^(s*scale*log2e - lse) (masked to 0), written
 //               to shared memory (fp16/bf16, 128-byte swizzle); dS = P (dP - delta) written
-//               likewise; dQ_i row added to an fp32 accumulator with vector reductions. At the
-//               end the same threads hold one key row each and write dK_j and dV_j.
+//               likewise; dQ_i staged in shared memory (fp32, in the then free P and dS
+//               buffers) and added into an fp32 accumulator by the TMA engine (bulk tensor
+//               reduce-add). At the end the same threads hold one key row each and write dK_j
+//               and dV_j.
 // Every wait is bounded.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -72,6 +74,7 @@ enum : int {
   SITE_DQ = 0x3b,
   SITE_DQFREE = 0x3c,
   SITE_ACC = 0x3d,
+  SITE_STAGE = 0x3e,
 };
 
 // Shared-memory tiles are 128 rows in 128-byte swizzle spans ("chunks" of 64 elements, each
@@ -91,6 +94,7 @@ struct Geo {
   static constexpr int BAR_OFF = DS_OFF + TILE_P;
   static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory plan");
+  static_assert(DS_OFF == P_OFF + TILE_P && 128 * D * 4 <= 2 * TILE_P, "dQ staging spans P and dS");
 };
 
 struct Args {
@@ -116,6 +120,22 @@ __device__ __forceinline__ uint64_t mndesc(uint32_t base, int k) {
   return make_sdesc(base + k * 16 * 128, 128 * 128, 1024, 2u);
 }
 
+// dQ partial tile -> fp32 accumulator in global memory: the TMA engine adds a 128-row x 32-column
+// box from shared memory (128-byte swizzle) into the tensor.
+__device__ __forceinline__ void tma_reduce_add_2d(const void *map, uint32_t src, int c0, int c1) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until the committed bulk operations have finished reading their shared memory.
+__device__ __forceinline__ void bulk_wait_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // Writes 128 values as one swizzled row of a 128-column tile (thread `row` owns row `row`).
 // (`v` holds fp32 bit patterns.)
 template <typename T>
@@ -138,7 +158,7 @@ template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                     const Args a) {
+                     const __grid_constant__ CUtensorMap tm_dq, const Args a) {
   using G = Geo<D>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr int CH = D / 64;  // 128-byte chunks per row of a D-column tile
@@ -159,7 +179,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *dq_full = bars + 10;
   uint64_t *dq_free = bars + 11;
   uint64_t *acc_done = bars + 12;
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 13);
+  uint64_t *stage_full = bars + 13;  // 128 row threads have staged dQ_i
+  uint64_t *stage_free = bars + 14;  // the TMA engine has read the staged dQ tile
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 15);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -187,6 +209,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(smem_u32(dq_full), 1);
     mbar_init(smem_u32(dq_free), 128);
     mbar_init(smem_u32(acc_done), 1);
+    mbar_init(smem_u32(stage_full), 128);
+    mbar_init(smem_u32(stage_free), 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm_q);
@@ -319,17 +343,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       // p holds S, then P, then dS (fp32 bits), one row per thread.
       uint32_t p[128];
       tmem_ld4x32(tmem_base + lane_off + S_COL, p);
+      const uint64_t scale2 = f2_pack(a.scale_log2, a.scale_log2);
+      const uint64_t nlse2 = f2_pack(-lse, -lse);
 #pragma unroll
-      for (int t = 0; t < 128; ++t) {
-        const int kg = j * BN + t;
-        const bool vis = rv && kg < a.Sk && !(a.causal && kg > qg);
-        p[t] = __float_as_uint(vis ? ex2_approx(fmaf(__uint_as_float(p[t]), a.scale_log2, -lse)) : 0.f);
+      for (int t = 0; t < 128; t += 2) {
+        float x0, x1;
+        f2_unpack(f2_fma(f2_pack(__uint_as_float(p[t]), __uint_as_float(p[t + 1])), scale2, nlse2), x0, x1);
+        p[t] = __float_as_uint(ex2_approx(x0));
+        p[t + 1] = __float_as_uint(ex2_approx(x1));
       }
-      // P's buffer is free once the previous step's dV GEMM has read it.
+      // Only tiles on the causal diagonal or at a ragged edge need the mask.
+      const bool full = (!a.causal || j * BN + BN - 1 <= i * BM) && (j + 1) * BN <= a.Sk &&
+                        (i + 1) * BM <= a.Sq;
+      if (!full) {
+#pragma unroll
+        for (int t = 0; t < 128; ++t) {
+          const int kg = j * BN + t;
+          if (!(rv && kg < a.Sk && !(a.causal && kg > qg))) p[t] = 0u;
+        }
+      }
+      // P's buffer is free once the previous step's dV GEMM has read it and the TMA engine
+      // has read the previous dQ tile staged there.
       if (it > 0 && !__all_sync(0xffffffffu, mbar_wait(smem_u32(p_free), par ^ 1, abort_flag, &g_fbwd_status,
                                                         TLLM_DEV_WAIT_TIMEOUT + SITE_PFREE))) {
         ok = false;
         break;
+      }
+      if (it > 0) {
+        if (threadIdx.x == 64) {
+          bulk_wait_read0();
+          mbar_arrive(smem_u32(stage_free));
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(stage_free), par ^ 1, abort_flag, &g_fbwd_status,
+                                               TLLM_DEV_WAIT_TIMEOUT + SITE_STAGE))) {
+          ok = false;
+          break;
+        }
       }
       store_row128<T>(smem + G::P_OFF, row, p);
       fence_proxy_async_smem();
@@ -361,23 +410,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      float *dqrow = a.dq_acc + (rowbase + qg) * D;
+      // Stage scale * dQ_i (fp32, zero for rows past Sq) in the P and dS buffers, both free
+      // once dQ_i is complete, as D/32 boxes of 128 rows x 32 columns (128-byte swizzle); one
+      // thread then has the TMA engine add them into the accumulator.
 #pragma unroll 1
       for (int c = 0; c < D; c += 32) {
         uint32_t r[32];
         tmem_ld32(tmem_base + lane_off + S_COL + c, r);
-        if (rv) {
+        uint8_t *box = smem + G::P_OFF + (c / 32) * (128 * 128) + row * 128;
 #pragma unroll
-          for (int t = 0; t < 32; t += 4)
-            asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dqrow + c + t),
-                         "f"(__uint_as_float(r[t]) * a.scale), "f"(__uint_as_float(r[t + 1]) * a.scale),
-                         "f"(__uint_as_float(r[t + 2]) * a.scale), "f"(__uint_as_float(r[t + 3]) * a.scale)
-                         : "memory");
+        for (int u = 0; u < 8; ++u) {
+          float4 f;
+          f.x = rv ? __uint_as_float(r[4 * u + 0]) * a.scale : 0.f;
+          f.y = rv ? __uint_as_float(r[4 * u + 1]) * a.scale : 0.f;
+          f.z = rv ? __uint_as_float(r[4 * u + 2]) * a.scale : 0.f;
+          f.w = rv ? __uint_as_float(r[4 * u + 3]) * a.scale : 0.f;
+          *reinterpret_cast<float4 *>(box + ((u ^ (row & 7)) << 4)) = f;
         }
       }
       tc_fence_before();
       mbar_arrive(smem_u32(dq_free));
+      fence_proxy_async_smem();
+      mbar_arrive(smem_u32(stage_full));
+      if (threadIdx.x == 64) {
+        if (!mbar_wait(smem_u32(stage_full), par, abort_flag, &g_fbwd_status,
+                       TLLM_DEV_WAIT_TIMEOUT + SITE_STAGE)) {
+          ok = false;
+        } else {
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c)
+            tma_reduce_add_2d(&tm_dq, sP + c * (128 * 128), c * 32, static_cast<int>(rowbase) + i * BM);
+          bulk_commit();
+        }
+      }
+      ok = __all_sync(0xffffffffu, ok);
     }
+    if (threadIdx.x == 64) bulk_wait_all();
     // ---- dK_j, dV_j: thread `row` holds key row j * BN + row ----
     const int kg = j * BN + row;
     const bool have = ok && n_it > 0 &&
@@ -478,6 +546,16 @@ int launch(const void *q, const void *k, const void *v, const void *o, const voi
     const uint64_t str[3] = {(uint64_t)s[2] * 2, (uint64_t)s[1] * 2, (uint64_t)s[0] * 2};
     return encode_tiled(m, dt, 4, const_cast<void *>(p), dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
   };
+  CUtensorMap mdq;
+  {
+    // fp32 accumulator [B*H*Sq, D], boxes of 128 rows x 32 columns
+    const uint64_t dims[2] = {(uint64_t)D, (uint64_t)(B * H * (Sq > 0 ? Sq : 1))};
+    const uint64_t str[1] = {(uint64_t)D * 4};
+    const uint32_t box2[2] = {32, 128};
+    int rc0 = encode_tiled(&mdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ws, dims, str, box2,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc0) return rc0;
+  }
   int rc = enc(&mq, q, Sq, sq);
   if (!rc) rc = enc(&mk, k, Sk, sk);
   if (!rc) rc = enc(&mv, v, Sk, sv);
@@ -513,7 +591,7 @@ int launch(const void *q, const void *k, const void *v, const void *o, const voi
     auto kern = flash_bwd_kernel<T, D>;
     TLLM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Gm::SMEM_BYTES));
     const unsigned grid = static_cast<unsigned>(B * H * a.n_ktiles);
-    kern<<<grid, kThreads, Gm::SMEM_BYTES, st>>>(mq, mk, mv, mdo, a);
+    kern<<<grid, kThreads, Gm::SMEM_BYTES, st>>>(mq, mk, mv, mdo, mdq, a);
     TLLM_CUDA_TRY(cudaGetLastError());
   }
   const int64_t n = rows * D;
@@ -553,7 +631,8 @@ extern "C" int tllm_flash_attn_bwd(const void *q, const void *k, const void *v, 
   if (B == 0 || H == 0 || (Sq == 0 && Sk == 0)) return TLLM_OK;
   TLLM_CHECK_ARG(q && k && v && o && dout && lse && dq && dk && dv,
                  "flash_attention_backward: null tensor pointer");
-  TLLM_CHECK_ARG(Sq < (1LL << 31) && Sk < (1LL << 31) && B * H * ((Sk + 127) / 128) < (1LL << 31),
+  TLLM_CHECK_ARG(Sq < (1LL << 31) && Sk < (1LL << 31) && B * H * ((Sk + 127) / 128) < (1LL << 31) &&
+                     B * H * Sq < (1LL << 31),
                  "flash_attention_backward: problem too large");
   const size_t need = tllm_flash_attn_bwd_workspace_size(B, H, Sq, D);
   TLLM_CHECK_ARG(Sq == 0 || (workspace && workspace_bytes >= need),
