@@ -226,6 +226,7 @@ OP_CASES = {
     "kv_append_rope": "paged_kv_append_rope B16 T2048 H8 D128 bs16 fp16",
     "flash_varlen": "flash_attention_varlen causal 16 sequences U[256,4096] H32 D128 fp16",
     "flash_bwd": "flash_attention_backward causal [4,32,4096,128] fp16",
+    "swiglu_fp8": "swiglu_fp8 e4m3 M4096 K4096 N14336, fp16 out",
 }
 
 
@@ -346,6 +347,14 @@ def run_op(args):
         q, k, v, cu, mx, work = _varlen_inputs(torch)
         fn = lambda: flash_attention_varlen(q, k, v, cu, cu, mx, mx, causal=True)  # noqa: E731
         unit = "TFLOP/s"
+    elif op == "swiglu_fp8":
+        from tritonllmcompiler_b200.ops.swiglu_fp8 import quantize_e4m3, swiglu_fp8
+        M, K, N = SWIGLU_SHAPE
+        x8, sx = quantize_e4m3(rn((M, K)))
+        w18, s1 = quantize_e4m3(rn((N, K), K ** -0.5))
+        w38, s3 = quantize_e4m3(rn((N, K), K ** -0.5))
+        fn = lambda: swiglu_fp8(x8, w18, w38, sx, s1, s3)  # noqa: E731
+        work, unit = 4.0 * M * K * N, "TFLOP/s"
     elif op == "flash_bwd":
         from tritonllmcompiler_b200.ops.flash_backward import flash_attention_backward, flash_attention_fwd_lse
         q, k, v, do = rn((4, 32, 4096, 128)), rn((4, 32, 4096, 128)), rn((4, 32, 4096, 128)), rn((4, 32, 4096, 128))
@@ -485,6 +494,21 @@ def extra_ops(torch, T, peaks):
         "value": tf, "unit": "TFLOP/s", "ms": t, "flops": flops, "roofline_frac": tf / tc,
         "bound": "tensor", "sm_mhz": clk.summary().get("sm_mhz")}
     del kc, vc
+    # FP8 (e4m3) swiglu at the headline shape (an extension: not the fp16 headline metric).
+    from tritonllmcompiler_b200.ops.swiglu_fp8 import quantize_e4m3, swiglu_fp8
+    M, K, N = SWIGLU_SHAPE
+    x8, sx = quantize_e4m3(gen((M, K), 7))
+    w18, s1 = quantize_e4m3(gen((N, K), 8, K ** -0.5))
+    w38, s3 = quantize_e4m3(gen((N, K), 9, K ** -0.5))
+    flops = 4.0 * M * K * N
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ts = _events_time(torch, lambda: swiglu_fp8(x8, w18, w38, sx, s1, s3), 20, 5, flush)
+    t = statistics.median(ts)
+    tf = flops / (t * 1e-3) / 1e12
+    res["swiglu_fp8_m4096_k4096_n14336"] = {"value": tf, "unit": "TFLOP/s", "ms": t, "flops": flops,
+                                            "roofline_frac_of_bf16_peak": tf / tc, "bound": "tensor",
+                                            "sm_mhz": clk.summary().get("sm_mhz")}
+    del x8, w18, w38
     # FlashAttention backward, causal [4,32,4096,128]: 2.5x the forward's FLOPs (five GEMMs
     # against two), the FlashAttention convention.
     from tritonllmcompiler_b200.ops.flash_backward import flash_attention_backward, flash_attention_fwd_lse

@@ -297,6 +297,18 @@ TLLM_API int tllm_flash_attn_bwd(const void *q, const void *k, const void *v, co
                                  const int64_t *sdv, float sm_scale, int causal, int dtype,
                                  void *stream);
 
+/*
+ * FP8 SwiGLU: out = silu(scale_x*scale_w1 * x@w1) * (scale_x*scale_w3 * x@w3) with e4m3 inputs
+ * and per-tensor scales, fp32 accumulation, fp16/bf16 output. An extension of tllm_swiglu
+ * (python/triton_llm/ops/swiglu.py:54-76 is fp16) on the tcgen05 kind::f8f6f4 path. x is
+ * [M, K] (lda), the weights are given transposed: w1t, w3t [N, K] (ldb1, ldb3), K contiguous;
+ * K and the input leading dimensions must be multiples of 16, inputs 16-byte aligned.
+ */
+TLLM_API int tllm_swiglu_fp8(const void *x, const void *w1t, const void *w3t, void *out,
+                             int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb1,
+                             int64_t ldb3, int64_t ldo, float scale_x, float scale_w1,
+                             float scale_w3, int out_dtype, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

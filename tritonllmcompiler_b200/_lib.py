@@ -95,6 +95,11 @@ SIGNATURES = {
          _i64, _i64, _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p, _c_i64p,
          ctypes.c_float, ctypes.c_int, ctypes.c_int, _vp],
     ),
+    "tllm_swiglu_fp8": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float,
+         ctypes.c_float, ctypes.c_float, ctypes.c_int, _vp],
+    ),
     "tllm_swiglu": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_int, _vp],

@@ -1,0 +1,333 @@
+// FP8 (e4m3) SwiGLU dual GEMM for sm_100a: out = silu(sx*s1 * x@w1) * (sx*s3 * x@w3).
+//
+// Extension of the reference's fp16 swiglu (python/triton_llm/ops/swiglu.py:54-76; oracle
+// python/triton_llm/reference/swiglu.py:12-15) to 8-bit inputs with per-tensor scales, the
+// tcgen05 kind::f8f6f4 path (twice the dense fp16 rate on B200). The weights are given
+// transposed, w1t/w3t [N, K] with K contiguous (the layout FP8 weights are usually stored
+// in), so both UMMA operands are K-major.
+//
+// Same structure as swiglu.cu: persistent, one CTA per SM; warp 0 TMA (x tile 128 x 128 bytes,
+// w1t and w3t tiles 128 x 128 bytes side by side -> one 256-row B operand), warp 1 issues
+// 128x256x32 UMMAs into double-buffered TMEM accumulators, warps 2-5 apply the scales,
+// silu(g)*u in fp32 and store fp16/bf16. Every wait is bounded.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <type_traits>
+
+#include "common.h"
+#include "ptx.cuh"
+
+namespace tllm {
+
+__device__ int g_swiglu8_status = 0;
+
+int swiglu8_read_status(int *out) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_swiglu8_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_status(e, "cudaMemcpyFromSymbol(swiglu fp8 status)");
+  const int zero = 0;
+  e = cudaMemcpyToSymbol(g_swiglu8_status, &zero, sizeof(int));
+  if (e != cudaSuccess) return cuda_status(e, "cudaMemcpyToSymbol(swiglu fp8 status)");
+  *out = v;
+  return TLLM_OK;
+}
+
+namespace swiglu8 {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 128;   // output columns per tile (each of w1 and w3)
+constexpr int BK = 128;   // one 128-byte swizzle row of e4m3
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK;          // 16 KB
+constexpr int B_BYTES = 2 * BN * BK;      // w1t rows then w3t rows: 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int ACC_COLS = 2 * BN;
+constexpr int TMEM_COLS = 512;
+constexpr int kThreads = 192;
+constexpr int kEpiThreads = 128;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 1024;
+
+enum : int { SITE_EMPTY = 0x41, SITE_FULL = 0x42, SITE_TEMPTY = 0x43, SITE_TFULL = 0x44 };
+
+struct Geom {
+  int M, N, K;
+  int tiles_m, tiles_n, k_blocks;
+  int64_t ldo;
+  int vec_store;
+  float scale_g, scale_u;  // sx * s1, sx * s3
+};
+
+__device__ __forceinline__ void umma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// kind::f8f6f4 instruction descriptor: fp32 accumulator, A and B e4m3 (format 0), both
+// K-major; N >> 3 and M >> 4 in their fields (the same bit layout as kind::f16).
+constexpr uint32_t idesc_e4m3(int M, int N) {
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    swiglu_fp8_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w1,
+                      const __grid_constant__ CUtensorMap tm_w3, T *__restrict__ out, const Geom g) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+  uint64_t *full = bars;
+  uint64_t *empty = bars + STAGES;
+  uint64_t *tfull = bars + 2 * STAGES;
+  uint64_t *tempty = bars + 2 * STAGES + 2;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), kEpiThreads);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_w1);
+    tma_prefetch_desc(&tm_w3);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const int num_tiles = g.tiles_m * g.tiles_n;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile % g.tiles_m) * BM;
+        const int n0 = (tile / g.tiles_m) * BN;
+        for (int kb = 0; kb < g.k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1, abort_flag, &g_swiglu8_status,
+                         TLLM_DEV_WAIT_TIMEOUT + SITE_EMPTY)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&full[stage]);
+          mbar_arrive_expect_tx(fb, STAGE_BYTES);
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+          const int k0 = kb * BK;
+          tma_load_2d(sa, &tm_x, fb, k0, m0);
+          tma_load_2d(sb, &tm_w1, fb, k0, n0);
+          tma_load_2d(sb + BN * BK, &tm_w3, fb, k0, n0);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_e4m3(BM, 2 * BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1, abort_flag, &g_swiglu8_status,
+                       TLLM_DEV_WAIT_TIMEOUT + SITE_TEMPTY)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
+        for (int kb = 0; kb < g.k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, &g_swiglu8_status,
+                         TLLM_DEV_WAIT_TIMEOUT + SITE_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k) {
+            // Both operands K-major, 128-byte swizzle, 8-row groups 1024 B apart; a k-step
+            // of 32 e4m3 elements is 32 bytes along the row.
+            const uint64_t adesc = make_sdesc(sa + k * 32, 16, 1024, kSwizzle128B);
+            const uint64_t bdesc = make_sdesc(sb + k * 32, 16, 1024, kSwizzle128B);
+            umma_f8_ss(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(smem_u32(&empty[stage]));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(&tfull[acc]));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag, &g_swiglu8_status,
+                     TLLM_DEV_WAIT_TIMEOUT + SITE_TFULL))
+        break;
+      tc_fence_after();
+      const int m0 = (tile % g.tiles_m) * BM;
+      const int n0 = (tile / g.tiles_m) * BN;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * ACC_COLS;
+      const int m = m0 + row;
+      T *orow = out + static_cast<int64_t>(m) * g.ldo;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t gr[32], ur[32];
+        tmem_ld32(t_row + c, gr);
+        tmem_ld32(t_row + BN + c, ur);
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float gv = __uint_as_float(gr[j]) * g.scale_g;
+          const float uv = __uint_as_float(ur[j]) * g.scale_u;
+          v[j] = (gv / (1.0f + expf(-gv))) * uv;
+        }
+        if (m < g.M) {
+          const int nb = n0 + c;
+          if (g.vec_store && nb + 32 <= g.N) {
+#pragma unroll
+            for (int jj = 0; jj < 32; jj += 8) {
+              uint4 raw;
+              raw.x = Pack2<T>::pack(v[jj + 0], v[jj + 1]);
+              raw.y = Pack2<T>::pack(v[jj + 2], v[jj + 3]);
+              raw.z = Pack2<T>::pack(v[jj + 4], v[jj + 5]);
+              raw.w = Pack2<T>::pack(v[jj + 6], v[jj + 7]);
+              *reinterpret_cast<uint4 *>(orow + nb + jj) = raw;
+            }
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj)
+              if (nb + jj < g.N) orow[nb + jj] = from_f32<T>(v[jj]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&tempty[acc]));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <typename T>
+int launch(const void *x, const void *w1t, const void *w3t, void *out, int64_t M, int64_t N,
+           int64_t K, int64_t lda, int64_t ldb1, int64_t ldb3, int64_t ldo, float scale_g,
+           float scale_u, cudaStream_t st) {
+  CUtensorMap mx, m1, m3;
+  const uint32_t box[2] = {BK, 128};
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+    const uint64_t str[1] = {static_cast<uint64_t>(lda)};
+    int rc = encode_tiled(&mx, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(x), dims, str,
+                          box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
+    const uint64_t s1[1] = {static_cast<uint64_t>(ldb1)};
+    int rc = encode_tiled(&m1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(w1t), dims, s1,
+                          box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    const uint64_t s3[1] = {static_cast<uint64_t>(ldb3)};
+    rc = encode_tiled(&m3, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(w3t), dims, s3, box,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  Geom g;
+  g.M = static_cast<int>(M);
+  g.N = static_cast<int>(N);
+  g.K = static_cast<int>(K);
+  g.tiles_m = static_cast<int>((M + BM - 1) / BM);
+  g.tiles_n = static_cast<int>((N + BN - 1) / BN);
+  g.k_blocks = static_cast<int>((K + BK - 1) / BK);
+  g.ldo = ldo;
+  g.vec_store = (ldo % 8 == 0 && aligned16(out)) ? 1 : 0;
+  g.scale_g = scale_g;
+  g.scale_u = scale_u;
+  const int num_tiles = g.tiles_m * g.tiles_n;
+  const int sms = sm_count();
+  const int grid = num_tiles < sms ? num_tiles : sms;
+  auto kern = swiglu_fp8_kernel<T>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(swiglu fp8)");
+  kern<<<grid, kThreads, SMEM_BYTES, st>>>(mx, m1, m3, static_cast<T *>(out), g);
+  return cuda_status(cudaGetLastError(), "swiglu fp8 launch");
+}
+
+}  // namespace
+}  // namespace swiglu8
+}  // namespace tllm
+
+extern "C" int tllm_swiglu_fp8(const void *x, const void *w1t, const void *w3t, void *out,
+                               int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb1,
+                               int64_t ldb3, int64_t ldo, float scale_x, float scale_w1,
+                               float scale_w3, int out_dtype, void *stream) {
+  using namespace tllm;
+  clear_error();
+  TLLM_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "swiglu_fp8: negative dimension");
+  TLLM_CHECK_ARG(out_dtype == TLLM_DTYPE_F16 || out_dtype == TLLM_DTYPE_BF16,
+                 "swiglu_fp8: unsupported output dtype %d", out_dtype);
+  TLLM_CHECK_ARG(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31), "swiglu_fp8: dimension too large");
+  if (M == 0 || N == 0) return TLLM_OK;
+  TLLM_CHECK_ARG(out && K > 0 && x && w1t && w3t, "swiglu_fp8: null pointer or K == 0");
+  TLLM_CHECK_ARG(lda >= K && ldb1 >= K && ldb3 >= K && ldo >= N, "swiglu_fp8: leading dimension too small");
+  TLLM_CHECK_ARG(K % 16 == 0 && lda % 16 == 0 && ldb1 % 16 == 0 && ldb3 % 16 == 0,
+                 "swiglu_fp8: K and the input leading dimensions must be multiples of 16 bytes");
+  TLLM_CHECK_ARG(swiglu8::aligned16(x) && swiglu8::aligned16(w1t) && swiglu8::aligned16(w3t),
+                 "swiglu_fp8: inputs must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float sg = scale_x * scale_w1, su = scale_x * scale_w3;
+  if (out_dtype == TLLM_DTYPE_F16)
+    return swiglu8::launch<__half>(x, w1t, w3t, out, M, N, K, lda, ldb1, ldb3, ldo, sg, su, st);
+  return swiglu8::launch<__nv_bfloat16>(x, w1t, w3t, out, M, N, K, lda, ldb1, ldb3, ldo, sg, su, st);
+}
