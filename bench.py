@@ -227,6 +227,7 @@ OP_CASES = {
     "flash_varlen": "flash_attention_varlen causal 16 sequences U[256,4096] H32 D128 fp16",
     "flash_bwd": "flash_attention_backward causal [4,32,4096,128] fp16",
     "swiglu_fp8": "swiglu_fp8 e4m3 M4096 K4096 N14336, fp16 out",
+    "qkv_norm_rope": "qkv_norm_rope M4096 K4096 Hq32 Hkv8 D128 fp16 (Llama-3-8B QKV)",
 }
 
 
@@ -306,6 +307,18 @@ def _varlen_inputs(torch, n=16, h=32, d=128, seed=6):
     return q, k, v, cu.cuda(), int(lens.max()), flops
 
 
+def _qkv_inputs(torch, rn, m=4096, k=4096, hq=32, hkv=8):
+    n = (hq + 2 * hkv) * 128
+    x, w = rn((m, k)), rn((k, n), k ** -0.5)
+    wq = (1 + 0.1 * torch.randn(128, device="cuda")).half()
+    wk = (1 + 0.1 * torch.randn(128, device="cuda")).half()
+    pos = torch.arange(8192, device="cuda", dtype=torch.float32)
+    inv = 1.0 / (10000 ** (torch.arange(0, 128, 2, device="cuda").float() / 128))
+    emb = torch.cat([torch.outer(pos, inv)] * 2, dim=-1)
+    positions = torch.arange(m, device="cuda", dtype=torch.int32)
+    return x, w, wq, wk, emb.cos().half(), emb.sin().half(), positions
+
+
 def run_op(args):
     """Runs one operator case warmup+steps times; prints {"op", "ms", "value", "unit"}."""
     import torch
@@ -347,6 +360,11 @@ def run_op(args):
         q, k, v, cu, mx, work = _varlen_inputs(torch)
         fn = lambda: flash_attention_varlen(q, k, v, cu, cu, mx, mx, causal=True)  # noqa: E731
         unit = "TFLOP/s"
+    elif op == "qkv_norm_rope":
+        from tritonllmcompiler_b200.ops.qkv_norm_rope import qkv_norm_rope
+        args_ = _qkv_inputs(torch, rn)
+        fn = lambda: qkv_norm_rope(*args_, num_q_heads=32, num_kv_heads=8)  # noqa: E731
+        work, unit = 2.0 * 4096 * 4096 * 6144, "TFLOP/s"
     elif op == "swiglu_fp8":
         from tritonllmcompiler_b200.ops.swiglu_fp8 import quantize_e4m3, swiglu_fp8
         M, K, N = SWIGLU_SHAPE
@@ -494,6 +512,18 @@ def extra_ops(torch, T, peaks):
         "value": tf, "unit": "TFLOP/s", "ms": t, "flops": flops, "roofline_frac": tf / tc,
         "bound": "tensor", "sm_mhz": clk.summary().get("sm_mhz")}
     del kc, vc
+    # QKV projection with RMSNorm + RoPE in the epilogue (Llama-3-8B: K 4096, 32 q and 8 kv heads).
+    from tritonllmcompiler_b200.ops.qkv_norm_rope import qkv_norm_rope
+    qa = _qkv_inputs(torch, lambda shape, scale=1.0: gen(shape, 11, scale))
+    flops = 2.0 * 4096 * 4096 * 6144
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ts = _events_time(torch, lambda: qkv_norm_rope(*qa, num_q_heads=32, num_kv_heads=8), 20, 5, flush)
+    t = statistics.median(ts)
+    tf = flops / (t * 1e-3) / 1e12
+    res["qkv_norm_rope_m4096_k4096_hq32_hkv8"] = {"value": tf, "unit": "TFLOP/s", "ms": t, "flops": flops,
+                                                  "roofline_frac": tf / tc, "bound": "tensor",
+                                                  "sm_mhz": clk.summary().get("sm_mhz")}
+    del qa
     # FP8 (e4m3) swiglu at the headline shape (an extension: not the fp16 headline metric).
     from tritonllmcompiler_b200.ops.swiglu_fp8 import quantize_e4m3, swiglu_fp8
     M, K, N = SWIGLU_SHAPE

@@ -309,6 +309,23 @@ TLLM_API int tllm_swiglu_fp8(const void *x, const void *w1t, const void *w3t, vo
                              int64_t ldb3, int64_t ldo, float scale_x, float scale_w1,
                              float scale_w3, int out_dtype, void *stream);
 
+/*
+ * QKV projection with RMSNorm + RoPE fused into its epilogue. No counterpart in the reference,
+ * which runs rmsnorm_rope (python/triton_llm/ops/rmsnorm_rope.py:51-75) as a separate pass over
+ * projected q/k. out [M, N] = x [M, K] @ w [K, N] with N = (Hq + 2*Hkv) * D laid out as
+ * [q heads | k heads | v heads] (D = 128); every q head (RMSNorm weight wq [D]) and k head
+ * (wk [D]) of token row m goes through tllm_rmsnorm_rope's arithmetic on the projection
+ * rounded to the I/O dtype, with cos/sin row positions[m] (cos/sin [rope_rows, D], row strides
+ * scos/ssin; positions int32 [M] on the device, clamped to the table); v heads are stored
+ * as projected. K and the leading dimensions must be multiples of 8, pointers 16-byte aligned.
+ */
+TLLM_API int tllm_qkv_norm_rope(const void *x, const void *w, const void *wq, const void *wk,
+                                const void *cos, const void *sin, int64_t rope_rows,
+                                int64_t scos, int64_t ssin, const int32_t *positions, void *out,
+                                int64_t M, int64_t K, int64_t Hq, int64_t Hkv, int64_t D,
+                                int64_t lda, int64_t ldw, int64_t ldo, float eps, int dtype,
+                                void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -100,6 +100,11 @@ SIGNATURES = {
         [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float,
          ctypes.c_float, ctypes.c_float, ctypes.c_int, _vp],
     ),
+    "tllm_qkv_norm_rope": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
+         _i64, _i64, _i64, ctypes.c_float, ctypes.c_int, _vp],
+    ),
     "tllm_swiglu": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_int, _vp],

@@ -105,6 +105,7 @@ int pkv_read_status(int *out);
 int ppf_read_status(int *out);
 int fbwd_read_status(int *out);
 int swiglu8_read_status(int *out);
+int qkv_read_status(int *out);
 namespace paged {
 int read_status(int *out);
 }
@@ -112,7 +113,7 @@ int read_status(int *out);
 int read_and_clear_device_status(int *out) {
   int (*readers[])(int *) = {flash_read_status, swiglu_read_status, paged::read_status,
                              selftest_read_status, pkv_read_status, ppf_read_status,
-                             fbwd_read_status, swiglu8_read_status};
+                             fbwd_read_status, swiglu8_read_status, qkv_read_status};
   int first = 0;
   for (auto rd : readers) {
     int v = 0;
