@@ -32,6 +32,7 @@
 #include <type_traits>
 
 #include "common.h"
+#include "paged_attention.cuh"
 #include "ptx.cuh"
 
 namespace tllm {
@@ -640,12 +641,29 @@ int launch_d(const void *q, const void *kc, const void *vc, void *o, void *ws, c
 }  // namespace ppf
 }  // namespace tllm
 
+namespace tllm {
+namespace ppf {
+namespace {
+// Single-token decode with one query head per KV head is the reference's decode: it goes to
+// the CUDA-core split-KV kernel, which reads each token's K/V row with vector loads (this
+// kernel is bound by TMA box issue on paged blocks and reaches less there; with several query
+// heads per KV head the tensor-core path here is the faster one).
+bool use_decode_path(int64_t Hq, int64_t Hkv, int64_t Sq, int64_t D) {
+  (void)D;
+  return Sq == 1 && Hq == Hkv;
+}
+}  // namespace
+}  // namespace ppf
+}  // namespace tllm
+
 extern "C" size_t tllm_paged_prefill_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
                                                     int64_t D, int64_t block_size,
                                                     int64_t max_blocks) {
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || D <= 0 || block_size <= 0 || max_blocks <= 0 ||
       Hq % Hkv != 0)
     return 0;
+  if (tllm::ppf::use_decode_path(Hq, Hkv, Sq, D))
+    return tllm::paged::plan(B, Hq, D, block_size, max_blocks, tllm::sm_count()).ws_bytes;
   return tllm::ppf::make_plan(B, Hq, Hkv, Sq, D, block_size, max_blocks, tllm::sm_count()).ws_bytes;
 }
 
@@ -684,6 +702,37 @@ extern "C" int tllm_paged_prefill(const void *q, const void *k_cache, const void
                    "paged_prefill: q/cache strides must be multiples of 8 elements");
   TLLM_CHECK_ARG(aligned16(q) && aligned16(k_cache) && aligned16(v_cache),
                  "paged_prefill: q and the caches must be 16-byte aligned");
+  if (use_decode_path(Hq, Hkv, Sq, D)) {
+    const paged::Plan dp = paged::plan(B, Hq, D, block_size, max_blocks, sm_count());
+    paged::Params p{};
+    p.q = q; p.k_cache = k_cache; p.v_cache = v_cache;
+    p.block_tables = block_tables; p.context_lens = context_lens; p.o = o;
+    p.B = B; p.H = Hq; p.D = D;
+    p.num_blocks = num_blocks;
+    p.block_size = static_cast<int>(block_size);
+    p.log2_bs = block_size == 16 ? 4 : (block_size == 32 ? 5 : 6);
+    p.max_tokens = static_cast<int>(dp.max_tokens);
+    p.chunk = static_cast<int>(dp.chunk);
+    p.num_splits = static_cast<int>(dp.num_splits);
+    p.sq0 = sq[0]; p.sq1 = sq[1]; p.sq3 = sq[3];
+    p.skc0 = skc[0]; p.skc1 = skc[1]; p.skc2 = skc[2]; p.skc3 = skc[3];
+    p.svc0 = svc[0]; p.svc1 = svc[1]; p.svc2 = svc[2]; p.svc3 = svc[3];
+    p.sbt0 = sbt[0]; p.sbt1 = sbt[1];
+    p.so0 = so[0]; p.so1 = so[1]; p.so3 = so[3];
+    p.sm_scale = sm_scale;
+    int rc = paged::validate(p);
+    if (rc) return rc;
+    if (dp.num_splits > 1) {
+      if (!workspace || workspace_bytes < dp.ws_bytes)
+        return fail(TLLM_ERR_WORKSPACE, "paged_prefill: workspace of %zu bytes needed, %zu given",
+                    dp.ws_bytes, workspace_bytes);
+      TLLM_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0,
+                     "paged_prefill: workspace must be 256-byte aligned");
+      p.ws_ml = static_cast<float *>(workspace);
+      p.ws_acc = reinterpret_cast<float *>(static_cast<char *>(workspace) + dp.ws_acc_offset);
+    }
+    return paged::run(p, dtype, static_cast<cudaStream_t>(stream));
+  }
   const Plan pl = make_plan(B, Hq, Hkv, Sq, D, block_size, max_blocks, sm_count());
   TLLM_CHECK_ARG(pl.items * pl.splits < (1LL << 31), "paged_prefill: grid too large");
   if (pl.splits > 1) {
