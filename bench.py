@@ -227,6 +227,7 @@ OP_CASES = {
     "flash_varlen": "flash_attention_varlen causal 16 sequences U[256,4096] H32 D128 fp16",
     "flash_bwd": "flash_attention_backward causal [4,32,4096,128] fp16",
     "swiglu_fp8": "swiglu_fp8 e4m3 M4096 K4096 N14336, fp16 out",
+    "flash_fp8_causal": "flash_attention_fp8 e4m3 causal [4,32,4096,128], fp16 out",
     "qkv_norm_rope": "qkv_norm_rope M4096 K4096 Hq32 Hkv8 D128 fp16 (Llama-3-8B QKV)",
 }
 
@@ -373,6 +374,11 @@ def run_op(args):
         w38, s3 = quantize_e4m3(rn((N, K), K ** -0.5))
         fn = lambda: swiglu_fp8(x8, w18, w38, sx, s1, s3)  # noqa: E731
         work, unit = 4.0 * M * K * N, "TFLOP/s"
+    elif op == "flash_fp8_causal":
+        from tritonllmcompiler_b200.ops.flash_fp8 import flash_attention_fp8, quantize_qkv_e4m3
+        q8, k8, vt8, s1, s2, s3 = quantize_qkv_e4m3(*(rn((4, 32, 4096, 128)) for _ in range(3)))
+        fn = lambda: flash_attention_fp8(q8, k8, vt8, s1, s2, s3, causal=True)  # noqa: E731
+        work, unit = 4.0 * 4 * 32 * 4096 * 4096 * 128 * 0.5, "TFLOP/s"
     elif op == "flash_bwd":
         from tritonllmcompiler_b200.ops.flash_backward import flash_attention_backward, flash_attention_fwd_lse
         q, k, v, do = rn((4, 32, 4096, 128)), rn((4, 32, 4096, 128)), rn((4, 32, 4096, 128)), rn((4, 32, 4096, 128))
@@ -539,6 +545,19 @@ def extra_ops(torch, T, peaks):
                                             "roofline_frac_of_bf16_peak": tf / tc, "bound": "tensor",
                                             "sm_mhz": clk.summary().get("sm_mhz")}
     del x8, w18, w38
+    # FP8 (e4m3) flash attention forward, causal [4,32,4096,128] (an extension).
+    from tritonllmcompiler_b200.ops.flash_fp8 import flash_attention_fp8, quantize_qkv_e4m3
+    q8, k8, vt8, s1, s2, s3 = quantize_qkv_e4m3(*(gen((4, 32, 4096, 128), s_) for s_ in (2, 3, 4)))
+    flops = 4.0 * 4 * 32 * 4096 * 4096 * 128 * 0.5
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ts = _events_time(torch, lambda: flash_attention_fp8(q8, k8, vt8, s1, s2, s3, causal=True),
+                          10, 3, flush)
+    t = statistics.median(ts)
+    tf = flops / (t * 1e-3) / 1e12
+    res["flash_fp8_causal_4x32x4096x128"] = {"value": tf, "unit": "TFLOP/s", "ms": t, "flops": flops,
+                                             "roofline_frac_of_bf16_peak": tf / tc, "bound": "tensor",
+                                             "sm_mhz": clk.summary().get("sm_mhz")}
+    del q8, k8, vt8
     # FlashAttention backward, causal [4,32,4096,128]: 2.5x the forward's FLOPs (five GEMMs
     # against two), the FlashAttention convention.
     from tritonllmcompiler_b200.ops.flash_backward import flash_attention_backward, flash_attention_fwd_lse

@@ -310,6 +310,22 @@ TLLM_API int tllm_swiglu_fp8(const void *x, const void *w1t, const void *w3t, vo
                              float scale_w3, int out_dtype, void *stream);
 
 /*
+ * FP8 flash attention forward: softmax(sm_scale * (scale_q q)(scale_k k)^T) (scale_v v) with
+ * e4m3 inputs and per-tensor scales, on the tcgen05 kind::f8f6f4 path; an extension of
+ * tllm_flash_attn_fwd (python/triton_llm/ops/flash_attention.py:107-133 is fp16/bf16), with the
+ * same top-left causal mask. q [B, H, Sq, D], k [B, H, Sk, D], and V transposed: vt
+ * [B, H, D, Sk] (keys contiguous); D 64 or 128; strides in elements, innermost 1, the others
+ * multiples of 16; inputs 16-byte aligned. o [B, H, Sq, D] in out_dtype (fp16 or bf16), any
+ * strides. P is rounded to e4m3 for the P V product; the row sums use it unrounded.
+ */
+TLLM_API int tllm_flash_attn_fp8_fwd(const void *q, const void *k, const void *vt, void *o,
+                                     int64_t B, int64_t H, int64_t Sq, int64_t Sk, int64_t D,
+                                     const int64_t *sq, const int64_t *sk, const int64_t *svt,
+                                     const int64_t *so, float sm_scale, float scale_q,
+                                     float scale_k, float scale_v, int causal, int out_dtype,
+                                     void *stream);
+
+/*
  * QKV projection with RMSNorm + RoPE fused into its epilogue. No counterpart in the reference,
  * which runs rmsnorm_rope (python/triton_llm/ops/rmsnorm_rope.py:51-75) as a separate pass over
  * projected q/k. out [M, N] = x [M, K] @ w [K, N] with N = (Hq + 2*Hkv) * D laid out as

@@ -166,6 +166,16 @@ def test_flash_noncontiguous_and_scale(cuda_device):
     assert out.is_contiguous()
 
 
+@pytest.mark.parametrize("causal", [False, True])
+def test_flash_empty_keys_is_nan(cuda_device, causal):
+    # Sk = 0 (torch hands the library null pointers for empty k/v): 0/0 in every row, as the
+    # reference kernel gives.
+    q = torch.randn(1, 2, 100, 64, generator=_gen(40)).half().cuda()
+    k = torch.empty(1, 2, 0, 64, dtype=torch.float16, device="cuda")
+    out = T.flash_attention(q, k, k, causal=causal)
+    assert out.shape == q.shape and torch.isnan(out).all()
+
+
 def test_flash_value_scaling_is_exact(cuda_device):
     g = _gen(32)
     q = torch.randn(2, 4, 1024, 128, generator=g).half().cuda()

@@ -22,8 +22,10 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 
 #include <algorithm>
+#include <cmath>
 #include <type_traits>
 
 #include "common.h"
@@ -105,6 +107,9 @@ struct Args {
   // the units of s * scale * log2(e), i.e. P = 2^(s * scale * log2(e) - lse). The backward
   // pass recomputes P from it.
   float *lse;
+  // e4m3 inputs: the output is (P V) / l times this (the scale of V); the scales of q and k
+  // are folded into scale_log2.
+  float out_scale;
 };
 
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[32]) { tmem_ld32(taddr, r); }
@@ -430,13 +435,20 @@ constexpr float kLazyRescaleLog2 = 8.0f;
 constexpr int kGroupHeads = 8;
 
 
-template <int D>
+// Shared memory of the two-tile kernel for head dim D and EB-byte inputs. A Q or K tile is
+// 128 rows of D * EB bytes in 128-byte-swizzled spans of SWB bytes; with 16-bit inputs a V
+// tile has the same shape, with e4m3 inputs it is V transposed (D rows of 128 keys, 128 B).
+template <int D, int EB = 2>
 struct GeoPP {
-  static constexpr int SWB = Geo<D>::SWB;
-  static constexpr int CHUNKS = Geo<D>::CHUNKS;
-  static constexpr int CHUNK_BYTES = Geo<D>::CHUNK_BYTES;
-  static constexpr int TILE_BYTES = Geo<D>::TILE_BYTES;
-  static constexpr uint32_t LAYOUT = Geo<D>::LAYOUT;
+  static constexpr int ROWB = D * EB;
+  static constexpr int SWB = ROWB >= 128 ? 128 : ROWB;
+  static constexpr int CHUNKS = ROWB / SWB;
+  static constexpr int CHUNK_ELEMS = SWB / EB;
+  static constexpr int CHUNK_BYTES = BM * SWB;
+  static constexpr int TILE_BYTES = BM * ROWB;
+  static constexpr uint32_t LAYOUT = SWB == 128 ? 2u : (SWB == 64 ? 4u : 6u);
+  static_assert(EB == 2 || (D * BN == TILE_BYTES && (D == 64 || D == 128)),
+                "e4m3 tiles: head dim 64 or 128");
   static constexpr int Q_OFF = 0;                       // two Q tiles
   static constexpr int K_OFF = Q_OFF + 2 * TILE_BYTES;  // two K slots
   static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;  // two V slots
@@ -514,18 +526,70 @@ __device__ __forceinline__ PPItem pp_item(const Args &a, int item) {
 // Readers of each work-stealing response: the UMMA lane and one lane per softmax warp.
 constexpr int kClcReaders = 1 + 8;
 
+// K-major operand (Q or K) of geometry G: step k of the reduction (32 bytes: 16 elements of
+// 16 bits or 32 of 8 bits).
+template <class G>
+__device__ __forceinline__ uint64_t kmajor_desc_g(uint32_t base, int k) {
+  const int byte = k * 32;
+  const uint32_t addr = base + (byte / G::SWB) * G::CHUNK_BYTES + (byte % G::SWB);
+  return make_sdesc(addr, 16, 8 * G::SWB, G::LAYOUT);
+}
+
+__device__ __forceinline__ void umma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem] with 8-bit A and B: four K elements per 32-bit TMEM column.
+__device__ __forceinline__ void umma_f8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// kind::f8f6f4 instruction descriptor: fp32 accumulator, A and B e4m3 (format 0), K-major.
+constexpr uint32_t idesc_e4m3(int M, int N) {
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Four floats to e4m3 (round to nearest even, saturating), the first in the lowest byte.
+__device__ __forceinline__ uint32_t pack4_e4m3(float p0, float p1, float p2, float p3) {
+  uint32_t r;
+  asm("{\n\t.reg .b16 lo, hi;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 lo, %2, %1;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 hi, %4, %3;\n\t"
+      "mov.b32 %0, {lo, hi};\n\t}"
+      : "=r"(r)
+      : "f"(p0), "f"(p1), "f"(p2), "f"(p3));
+  return r;
+}
+
 // kSteal: the CTA keeps its TMEM, barriers and descriptors and moves on to further items. While
 // an item's last key/value tiles are in flight, the producer cancels the launch of the next CTA
 // that has not started (cluster launch control) and the CTA takes over that CTA's item, so
 // items still run in launch order, each on the first SM to free up, without a CTA launch and
 // set-up between them; the next item's Q tiles, first key tiles and first S overlap the
 // current item's epilogue.
-template <typename T, int D, bool kSteal, bool kVarlen>
+// TI: the input element type (T, or __nv_fp8_e4m3 with T the output type). With e4m3 inputs
+// tm_v maps V transposed ([.., D, Sk], keys contiguous), so that both UMMA operands of P V are
+// K-major, and P is stored to TMEM as e4m3, four keys per column.
+template <typename T, typename TI, int D, bool kSteal, bool kVarlen>
 __global__ void __launch_bounds__(kPPThreads, 1)
     flash_pp_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const Args a) {
-  using G = GeoPP<D>;
+  constexpr bool kF8 = std::is_same<TI, __nv_fp8_e4m3>::value;
+  static_assert(!kF8 || !kVarlen, "e4m3 inputs: dense batches only");
+  using G = GeoPP<D, kF8 ? 1 : 2>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr int OC = D < 32 ? D : 32;
   extern __shared__ uint8_t smem_raw[];
@@ -619,7 +683,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
 #pragma unroll
             for (int c = 0; c < G::CHUNKS; ++c)
               tma_load_4d(sQ + X * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_q, qb,
-                          c * (G::SWB / 2), w.qrow + w.q0 + X * BM, w.h, w.bc);
+                          c * G::CHUNK_ELEMS, w.qrow + w.q0 + X * BM, w.h, w.bc);
           }
           ++nq;
           for (int j = 0; j < w.n_kv; ++j, ++g) {
@@ -635,7 +699,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
 #pragma unroll
             for (int c = 0; c < G::CHUNKS; ++c)
               tma_load_4d(sK + s * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_k, kb,
-                          c * (G::SWB / 2), w.krow + j * BN, w.hk, w.bc);
+                          c * G::CHUNK_ELEMS, w.krow + j * BN, w.hk, w.bc);
             if (!mbar_wait(smem_u32(&v_empty[s]), par, abort_flag, &g_flash_status,
                            TLLM_DEV_WAIT_TIMEOUT + SITE_VEMPTY)) {
               ok = false;
@@ -643,10 +707,15 @@ __global__ void __launch_bounds__(kPPThreads, 1)
             }
             const uint32_t vb = smem_u32(&v_full[s]);
             mbar_arrive_expect_tx(vb, G::TILE_BYTES);
+            if constexpr (kF8) {
+              // One box of V transposed: 128 keys (x, a multiple of 128) of all D rows.
+              tma_load_4d(sV + s * G::TILE_BYTES, &tm_v, vb, j * BN, 0, w.hk, w.bc);
+            } else {
 #pragma unroll
-            for (int c = 0; c < G::CHUNKS; ++c)
-              tma_load_4d(sV + s * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_v, vb,
-                          c * (G::SWB / 2), w.krow + j * BN, w.hk, w.bc);
+              for (int c = 0; c < G::CHUNKS; ++c)
+                tma_load_4d(sV + s * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_v, vb,
+                            c * G::CHUNK_ELEMS, w.krow + j * BN, w.hk, w.bc);
+            }
           }
         }
         if (!ok || !kSteal) break;
@@ -664,15 +733,20 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   } else if (warp == 1) {
     // ------------------------------ UMMA issuer -------------------------------
     if (lane == 0) {
-      const uint32_t idesc_qk = make_idesc_f16(BM, BN, kBF16, false, false);
-      const uint32_t idesc_pv = make_idesc_f16(BM, D, kBF16, false, true);
+      const uint32_t idesc_qk = kF8 ? idesc_e4m3(BM, BN) : make_idesc_f16(BM, BN, kBF16, false, false);
+      const uint32_t idesc_pv = kF8 ? idesc_e4m3(BM, D) : make_idesc_f16(BM, D, kBF16, false, true);
       auto issue_qk = [&](int X, int kslot) {
         const uint32_t kbase = sK + kslot * G::TILE_BYTES;
         const uint32_t qbase = sQ + X * G::TILE_BYTES;
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k)
-          umma_f16_ss(tmem_base + X * BN, kmajor_desc<D>(qbase, k), kmajor_desc<D>(kbase, k),
-                      idesc_qk, k != 0 ? 1u : 0u);
+        for (int k = 0; k < G::ROWB / 32; ++k) {
+          if constexpr (kF8)
+            umma_f8_ss(tmem_base + X * BN, kmajor_desc_g<G>(qbase, k), kmajor_desc_g<G>(kbase, k),
+                       idesc_qk, k != 0 ? 1u : 0u);
+          else
+            umma_f16_ss(tmem_base + X * BN, kmajor_desc<D>(qbase, k), kmajor_desc<D>(kbase, k),
+                        idesc_qk, k != 0 ? 1u : 0u);
+        }
         umma_commit(smem_u32(&s_full[X]));
       };
       int item = static_cast<int>(blockIdx.x);
@@ -719,11 +793,19 @@ __global__ void __launch_bounds__(kPPThreads, 1)
               tc_fence_after();
               const uint32_t p_tmem = tmem_base + X * BN;
               const uint32_t o_tmem = tmem_base + O_COL + X * BN;
+              if constexpr (kF8) {
+                // B = V transposed: D rows of 128 keys (one 128-byte span); 32 keys a step.
 #pragma unroll
-              for (int k = 0; k < BN / 16; ++k) {
-                const uint64_t bdesc =
-                    make_sdesc(vbase + k * 16 * G::SWB, G::CHUNK_BYTES, 8 * G::SWB, G::LAYOUT);
-                umma_f16_ts(o_tmem, p_tmem + k * 8, bdesc, idesc_pv, (j | k) != 0 ? 1u : 0u);
+                for (int k = 0; k < BN / 32; ++k)
+                  umma_f8_ts(o_tmem, p_tmem + k * 8, make_sdesc(vbase + k * 32, 16, 1024, 2u),
+                             idesc_pv, (j | k) != 0 ? 1u : 0u);
+              } else {
+#pragma unroll
+                for (int k = 0; k < BN / 16; ++k) {
+                  const uint64_t bdesc =
+                      make_sdesc(vbase + k * 16 * G::SWB, G::CHUNK_BYTES, 8 * G::SWB, G::LAYOUT);
+                  umma_f16_ts(o_tmem, p_tmem + k * 8, bdesc, idesc_pv, (j | k) != 0 ? 1u : 0u);
+                }
               }
               if (j == w.nkv[X] - 1) {
                 umma_commit(smem_u32(&o_done[X]));
@@ -823,20 +905,42 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         uint64_t ps2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
         for (int hlf = 0; hlf < 2; ++hlf) {
-          uint32_t pk[32];
+          if constexpr (kF8) {
+            // e4m3 P: keys 64*hlf .. +63 in 16 columns.
+            uint32_t pk[16];
 #pragma unroll
-          for (int t = 0; t < 64; t += 2) {
-            const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sr[64 * hlf + t]),
-                                               __uint_as_float(sr[64 * hlf + t + 1])),
-                                       scale2, negm2);
-            float x0, x1;
-            f2_unpack(x2, x0, x1);
-            const float p0 = ex2_approx(x0);
-            const float p1 = ex2_approx(x1);
-            ps2[(t >> 1) & 3] = f2_add(ps2[(t >> 1) & 3], f2_pack(p0, p1));
-            pk[t >> 1] = Pack2<T>::pack(p0, p1);
+            for (int t = 0; t < 64; t += 4) {
+              float pv[4];
+#pragma unroll
+              for (int u = 0; u < 4; u += 2) {
+                const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sr[64 * hlf + t + u]),
+                                                   __uint_as_float(sr[64 * hlf + t + u + 1])),
+                                           scale2, negm2);
+                float x0, x1;
+                f2_unpack(x2, x0, x1);
+                pv[u] = ex2_approx(x0);
+                pv[u + 1] = ex2_approx(x1);
+                ps2[((t + u) >> 1) & 3] = f2_add(ps2[((t + u) >> 1) & 3], f2_pack(pv[u], pv[u + 1]));
+              }
+              pk[t >> 2] = pack4_e4m3(pv[0], pv[1], pv[2], pv[3]);
+            }
+            tmem_st16(s_tm + 16 * hlf, pk);
+          } else {
+            uint32_t pk[32];
+#pragma unroll
+            for (int t = 0; t < 64; t += 2) {
+              const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sr[64 * hlf + t]),
+                                                 __uint_as_float(sr[64 * hlf + t + 1])),
+                                         scale2, negm2);
+              float x0, x1;
+              f2_unpack(x2, x0, x1);
+              const float p0 = ex2_approx(x0);
+              const float p1 = ex2_approx(x1);
+              ps2[(t >> 1) & 3] = f2_add(ps2[(t >> 1) & 3], f2_pack(p0, p1));
+              pk[t >> 1] = Pack2<T>::pack(p0, p1);
+            }
+            tmem_st32(s_tm + 32 * hlf, pk);
           }
-          tmem_st32(s_tm + 32 * hlf, pk);
         }
         float psa, psb, psc, psd, pse, psf, psg, psh;
         f2_unpack(ps2[0], psa, psb);
@@ -868,7 +972,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           break;
         ++nod;
         tc_fence_after();
-        const float inv_l = 1.0f / l_run;
+        float inv_l = 1.0f / l_run;
+        if constexpr (kF8) inv_l *= a.out_scale;
         if (!kVarlen && a.lse != nullptr && qg < w.Sq)
           a.lse[(static_cast<int64_t>(w.b) * a.H + w.h) * a.Sq + qg] = m_use + log2f(l_run);
         T *orow = static_cast<T *>(a.o) + w.b * a.so0 + w.h * a.so1 +
@@ -935,6 +1040,43 @@ struct VarlenDesc {
   int64_t total_q, total_k, Hkv;
 };
 
+// Scheduling groups of the two-tile kernel: kGroupHeads heads per group, or all heads in one
+// group when a causal grid is only a few waves long (its tail then comes from the lightest
+// items of all heads); at most 64 MiB of K and V per group; sizes as even as possible.
+void set_groups(Args &a, int64_t B, int64_t H, int64_t Sk, int64_t row_bytes, int causal) {
+  const int64_t bh = B * H;
+  const int64_t n_pairs = (a.n_qtiles + 1) / 2;
+  const int64_t sms = sm_count() > 0 ? sm_count() : 148;
+  const int64_t kv_head_bytes = 2 * (Sk > 0 ? Sk : 1) * row_bytes;
+  int64_t target = (causal && bh * n_pairs <= 4 * sms) ? bh : kGroupHeads;
+  target = std::min<int64_t>(target, std::max<int64_t>(1, (64ll << 20) / kv_head_bytes));
+  const int64_t n_groups = (bh + target - 1) / target;
+  a.group = static_cast<int>(bh / n_groups);
+  a.n_small = static_cast<int>(n_groups - bh % n_groups);
+}
+
+// Launches a two-tile kernel instance after checking that the register split fits.
+template <class GP, typename K>
+int launch_pp(K kern, unsigned grid, const CUtensorMap &mq, const CUtensorMap &mk,
+              const CUtensorMap &mv, const Args &a, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GP::SMEM_BYTES);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(flash pp)");
+  // setmaxnreg.inc only completes if the launch holds the registers the split assumes.
+  cudaFuncAttributes fattr;
+  e = cudaFuncGetAttributes(&fattr, kern);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncGetAttributes(flash pp)");
+  if (fattr.numRegs != kPPRegsLaunch)
+    return fail(TLLM_ERR_CUDA, "flash_attention: kernel built with %d registers, %d expected",
+                fattr.numRegs, kPPRegsLaunch);
+  int resident = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kern, kPPThreads, GP::SMEM_BYTES);
+  if (e != cudaSuccess) return cuda_status(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor(flash pp)");
+  if (resident < 1)
+    return fail(TLLM_ERR_CUDA, "flash_attention: the two-tile kernel cannot be resident on this device");
+  kern<<<grid, kPPThreads, GP::SMEM_BYTES, st>>>(mq, mk, mv, a);
+  return cuda_status(cudaGetLastError(), "flash pp launch");
+}
+
 template <typename T, int D>
 int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, int64_t H,
              int64_t Sq, int64_t Sk, const int64_t *sq, const int64_t *sk, const int64_t *sv,
@@ -989,21 +1131,8 @@ int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, in
   a.G = vl ? static_cast<int>(H / vl->Hkv) : 1;
   a.total_q = vl ? static_cast<int>(vl->total_q) : 0;
   a.total_k = vl ? static_cast<int>(vl->total_k) : 0;
-  {
-    // Scheduling groups of the two-tile kernel: kGroupHeads heads per group, or all heads in
-    // one group when a causal grid is only a few waves long (its tail then comes from the
-    // lightest items of all heads); at most 64 MiB of K and V per group; sizes as even as
-    // possible.
-    const int64_t bh = B * H;
-    const int64_t n_pairs = (a.n_qtiles + 1) / 2;
-    const int64_t sms = sm_count() > 0 ? sm_count() : 148;
-    const int64_t kv_head_bytes = 2 * (Sk > 0 ? Sk : 1) * static_cast<int64_t>(D) * 2;
-    int64_t target = (causal && bh * n_pairs <= 4 * sms) ? bh : kGroupHeads;
-    target = std::min<int64_t>(target, std::max<int64_t>(1, (64ll << 20) / kv_head_bytes));
-    const int64_t n_groups = (bh + target - 1) / target;
-    a.group = static_cast<int>(bh / n_groups);
-    a.n_small = static_cast<int>(n_groups - bh % n_groups);
-  }
+  a.out_scale = 1.0f;
+  set_groups(a, B, H, Sk, D * 2, causal);
   if (variant == kVariantSingleTile && !vl) {
     auto kern = flash_fwd_kernel<T, D>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
@@ -1013,26 +1142,67 @@ int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, in
     return cuda_status(cudaGetLastError(), "flash launch");
   }
   using GP = GeoPP<D>;
-  auto kern = vl ? flash_pp_kernel<T, D, true, true>
-                : (variant == kVariantPingPongOneItem ? flash_pp_kernel<T, D, false, false>
-                                                      : flash_pp_kernel<T, D, true, false>);
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GP::SMEM_BYTES);
-  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(flash pp)");
-  // setmaxnreg.inc only completes if the launch holds the registers the split assumes.
-  cudaFuncAttributes fattr;
-  e = cudaFuncGetAttributes(&fattr, kern);
-  if (e != cudaSuccess) return cuda_status(e, "cudaFuncGetAttributes(flash pp)");
-  if (fattr.numRegs != kPPRegsLaunch)
-    return fail(TLLM_ERR_CUDA, "flash_attention: kernel built with %d registers, %d expected",
-                fattr.numRegs, kPPRegsLaunch);
-  int resident = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kern, kPPThreads, GP::SMEM_BYTES);
-  if (e != cudaSuccess) return cuda_status(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor(flash pp)");
-  if (resident < 1)
-    return fail(TLLM_ERR_CUDA, "flash_attention: the two-tile kernel cannot be resident on this device");
+  auto kern = vl ? flash_pp_kernel<T, T, D, true, true>
+                : (variant == kVariantPingPongOneItem ? flash_pp_kernel<T, T, D, false, false>
+                                                      : flash_pp_kernel<T, T, D, true, false>);
   const unsigned grid = static_cast<unsigned>(B * H * ((a.n_qtiles + 1) / 2));
-  kern<<<grid, kPPThreads, GP::SMEM_BYTES, st>>>(mq, mk, mv, a);
-  return cuda_status(cudaGetLastError(), "flash pp launch");
+  return launch_pp<GP>(kern, grid, mq, mk, mv, a, st);
+}
+
+// e4m3 q, k [B, H, S, D] and V transposed vt [B, H, D, Sk] (keys contiguous); strides in
+// elements (= bytes).
+template <typename T, int D>
+int launch_fp8(const void *q, const void *k, const void *vt, void *o, int64_t B, int64_t H,
+               int64_t Sq, int64_t Sk, const int64_t *sq, const int64_t *sk, const int64_t *svt,
+               const int64_t *so, float sm_scale, float scale_q, float scale_k, float scale_v,
+               int causal, cudaStream_t st) {
+  using GP = GeoPP<D, 1>;
+  const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const CUtensorMapSwizzle sw = GP::SWB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const uint32_t box[4] = {static_cast<uint32_t>(GP::SWB), static_cast<uint32_t>(BM), 1, 1};
+  CUtensorMap mq, mk, mv;
+  {
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)Sq, (uint64_t)H, (uint64_t)B};
+    const uint64_t str[3] = {(uint64_t)sq[2], (uint64_t)sq[1], (uint64_t)sq[0]};
+    int rc = encode_tiled(&mq, dt, 4, const_cast<void *>(q), dims, str, box, sw);
+    if (rc) return rc;
+  }
+  const uint64_t sk_ext = static_cast<uint64_t>(Sk > 0 ? Sk : 1);
+  {
+    const uint64_t dims[4] = {(uint64_t)D, sk_ext, (uint64_t)H, (uint64_t)B};
+    const uint64_t str[3] = {(uint64_t)sk[2], (uint64_t)sk[1], (uint64_t)sk[0]};
+    int rc = encode_tiled(&mk, dt, 4, const_cast<void *>(k), dims, str, box, sw);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[4] = {sk_ext, (uint64_t)D, (uint64_t)H, (uint64_t)B};
+    const uint64_t str[3] = {(uint64_t)svt[2], (uint64_t)svt[1], (uint64_t)svt[0]};
+    const uint32_t vbox[4] = {static_cast<uint32_t>(BN), static_cast<uint32_t>(D), 1, 1};
+    int rc = encode_tiled(&mv, dt, 4, const_cast<void *>(vt), dims, str, vbox,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  Args a{};
+  a.o = o;
+  a.so0 = so[0];
+  a.so1 = so[1];
+  a.so2 = so[2];
+  a.so3 = so[3];
+  a.H = static_cast<int>(H);
+  a.Sq = static_cast<int>(Sq);
+  a.Sk = static_cast<int>(Sk);
+  a.n_qtiles = static_cast<int>((Sq + BM - 1) / BM);
+  a.scale_log2 = sm_scale * scale_q * scale_k * kLog2e;
+  a.causal = causal ? 1 : 0;
+  a.vec_store = (so[3] == 1 && so[0] % 8 == 0 && so[1] % 8 == 0 && so[2] % 8 == 0 && aligned16(o)) ? 1 : 0;
+  a.lse = nullptr;
+  a.cu_q = nullptr;
+  a.cu_k = nullptr;
+  a.G = 1;
+  a.out_scale = scale_v;
+  set_groups(a, B, H, Sk, D, causal);
+  const unsigned grid = static_cast<unsigned>(B * H * ((a.n_qtiles + 1) / 2));
+  return launch_pp<GP>(flash_pp_kernel<T, __nv_fp8_e4m3, D, true, false>, grid, mq, mk, mv, a, st);
 }
 
 template <typename T>
@@ -1071,6 +1241,12 @@ int entry(const void *q, const void *k, const void *v, void *o, int64_t B, int64
                  "flash_attention: unknown kernel variant %d", variant);
   TLLM_CHECK_ARG(sq && sk && sv && so, "flash_attention: null stride array");
   if (B == 0 || H == 0 || Sq == 0) return TLLM_OK;
+  if (Sk == 0) {
+    // No keys (empty k/v may come as null pointers): every row is 0/0 = NaN, as in the
+    // reference kernel. The key/value maps are built over q and never read.
+    k = v = q;
+    sk = sv = sq;
+  }
   TLLM_CHECK_ARG(q && k && v && o, "flash_attention: null tensor pointer");
   TLLM_CHECK_ARG(Sq < (1LL << 31) && Sk < (1LL << 31) && B * H < (1LL << 31),
                  "flash_attention: problem too large");
@@ -1181,4 +1357,56 @@ extern "C" int tllm_flash_attn_varlen_fwd(const void *q, const void *k, const vo
                           sm_scale, causal, kVariantPingPong, st, &vl);
   return launch<__nv_bfloat16>(q, k, v, o, B, H, max_seqlen_q, max_seqlen_k, D, sq4, sk4, sv4,
                                so4, sm_scale, causal, kVariantPingPong, st, &vl);
+}
+
+// FP8 (e4m3) inputs with per-tensor scales (no counterpart in the reference, whose
+// flash_attention is fp16/bf16): softmax(sm_scale * (scale_q q)(scale_k k)^T) (scale_v v),
+// causal top-left aligned as in flash_attention. q, k: [B, H, Sq|Sk, D]; vt: V transposed,
+// [B, H, D, Sk] (keys contiguous); strides in elements, innermost 1, the others multiples of
+// 16; o: [B, H, Sq, D] fp16 or bf16 (out_dtype). P is rounded to e4m3 for the P V product.
+extern "C" int tllm_flash_attn_fp8_fwd(const void *q, const void *k, const void *vt, void *o,
+                                       int64_t B, int64_t H, int64_t Sq, int64_t Sk, int64_t D,
+                                       const int64_t *sq, const int64_t *sk, const int64_t *svt,
+                                       const int64_t *so, float sm_scale, float scale_q,
+                                       float scale_k, float scale_v, int causal, int out_dtype,
+                                       void *stream) {
+  using namespace tllm;
+  using namespace tllm::flash;
+  clear_error();
+  TLLM_CHECK_ARG(B >= 0 && H >= 0 && Sq >= 0 && Sk >= 0, "flash_attention_fp8: negative dimension");
+  TLLM_CHECK_ARG(D == 64 || D == 128, "flash_attention_fp8: head dim %lld not in {64,128}",
+                 (long long)D);
+  TLLM_CHECK_ARG(out_dtype == TLLM_DTYPE_F16 || out_dtype == TLLM_DTYPE_BF16,
+                 "flash_attention_fp8: unsupported output dtype %d", out_dtype);
+  TLLM_CHECK_ARG(sq && sk && svt && so, "flash_attention_fp8: null stride array");
+  if (B == 0 || H == 0 || Sq == 0) return TLLM_OK;
+  if (Sk == 0) {
+    // No keys: NaN rows, as tllm_flash_attn_fwd; the key maps are built over q, never read.
+    k = vt = q;
+    sk = svt = sq;
+  }
+  TLLM_CHECK_ARG(q && k && vt && o, "flash_attention_fp8: null tensor pointer");
+  TLLM_CHECK_ARG(Sq < (1LL << 31) && Sk < (1LL << 31) && B * H < (1LL << 31) &&
+                     B * H * ((Sq + 255) / 256) < (1LL << 31),
+                 "flash_attention_fp8: problem too large");
+  TLLM_CHECK_ARG(sq[3] == 1 && sk[3] == 1 && svt[3] == 1,
+                 "flash_attention_fp8: q/k/vt need a unit innermost stride");
+  for (int i = 0; i < 3; ++i)
+    TLLM_CHECK_ARG(sq[i] % 16 == 0 && sk[i] % 16 == 0 && svt[i] % 16 == 0,
+                   "flash_attention_fp8: q/k/vt strides must be multiples of 16 elements");
+  TLLM_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(vt),
+                 "flash_attention_fp8: q/k/vt must be 16-byte aligned");
+  TLLM_CHECK_ARG(std::isfinite(scale_q) && std::isfinite(scale_k) && std::isfinite(scale_v) &&
+                     scale_q > 0.f && scale_k > 0.f && scale_v > 0.f,
+                 "flash_attention_fp8: scales must be positive and finite");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (out_dtype == TLLM_DTYPE_F16)
+    return D == 64 ? launch_fp8<__half, 64>(q, k, vt, o, B, H, Sq, Sk, sq, sk, svt, so, sm_scale,
+                                            scale_q, scale_k, scale_v, causal, st)
+                   : launch_fp8<__half, 128>(q, k, vt, o, B, H, Sq, Sk, sq, sk, svt, so, sm_scale,
+                                             scale_q, scale_k, scale_v, causal, st);
+  return D == 64 ? launch_fp8<__nv_bfloat16, 64>(q, k, vt, o, B, H, Sq, Sk, sq, sk, svt, so,
+                                                 sm_scale, scale_q, scale_k, scale_v, causal, st)
+                 : launch_fp8<__nv_bfloat16, 128>(q, k, vt, o, B, H, Sq, Sk, sq, sk, svt, so,
+                                                  sm_scale, scale_q, scale_k, scale_v, causal, st);
 }
