@@ -437,7 +437,8 @@ constexpr int kGroupHeads = 8;
 
 // Shared memory of the two-tile kernel for head dim D and EB-byte inputs. A Q or K tile is
 // 128 rows of D * EB bytes in 128-byte-swizzled spans of SWB bytes; with 16-bit inputs a V
-// tile has the same shape, with e4m3 inputs it is V transposed (D rows of 128 keys, 128 B).
+// tile has the same shape, with e4m3 inputs it is V transposed (D rows of 128 keys, 128 B)
+// and each query tile also has a P tile in shared memory (128 rows of 128 e4m3 keys).
 template <int D, int EB = 2>
 struct GeoPP {
   static constexpr int ROWB = D * EB;
@@ -452,11 +453,13 @@ struct GeoPP {
   static constexpr int Q_OFF = 0;                       // two Q tiles
   static constexpr int K_OFF = Q_OFF + 2 * TILE_BYTES;  // two K slots
   static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;  // two V slots
-  static constexpr int BAR_OFF = V_OFF + 2 * TILE_BYTES;
+  static constexpr int P_OFF = V_OFF + 2 * TILE_BYTES;  // e4m3: two P tiles
+  static constexpr int P_TILE_BYTES = BM * BN;
+  static constexpr int BAR_OFF = P_OFF + (EB == 1 ? 2 * P_TILE_BYTES : 0);
   static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
 };
 
-enum : int { SITE_PFULL = 9, SITE_ODONE = 10, SITE_QEMPTY = 11, SITE_CLC = 12 };
+enum : int { SITE_PFULL = 9, SITE_ODONE = 10, SITE_QEMPTY = 11, SITE_CLC = 12, SITE_SFREE = 13 };
 
 // One work item of the two-tile kernel: query rows [q0, q0 + 2*BM) of head (b, h) and the
 // number of key tiles each of its two query tiles visits.
@@ -545,15 +548,11 @@ __device__ __forceinline__ void umma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uin
       : "memory");
 }
 
-// D[tmem] (+)= A[tmem] * B[smem] with 8-bit A and B: four K elements per 32-bit TMEM column.
-__device__ __forceinline__ void umma_f8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                           uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+// 16 bytes to shared memory.
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
 }
 
 // kind::f8f6f4 instruction descriptor: fp32 accumulator, A and B e4m3 (format 0), K-major.
@@ -581,7 +580,9 @@ __device__ __forceinline__ uint32_t pack4_e4m3(float p0, float p1, float p2, flo
 // current item's epilogue.
 // TI: the input element type (T, or __nv_fp8_e4m3 with T the output type). With e4m3 inputs
 // tm_v maps V transposed ([.., D, Sk], keys contiguous), so that both UMMA operands of P V are
-// K-major, and P is stored to TMEM as e4m3, four keys per column.
+// K-major, and P goes through shared memory as e4m3 (16 KB per query tile): the softmax frees
+// S_X as soon as it has loaded it, so QK_X(j+1) runs on the tensor core while P_X(j) is being
+// computed, instead of after PV_X(j).
 template <typename T, typename TI, int D, bool kSteal, bool kVarlen>
 __global__ void __launch_bounds__(kPPThreads, 1)
     flash_pp_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -610,6 +611,9 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 20);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
   const uint32_t clc_resp = smem_u32(bars + 22);  // two 16-byte responses
+  // e4m3 only: S_X has been read into registers (the next QK_X may overwrite it); o_done then
+  // completes after every PV_X (P_X in shared memory and O_X may be reused).
+  uint64_t *s_free = bars + 26;    // [2] per tile
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -627,6 +631,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       mbar_init(smem_u32(&o_done[s]), 1);
       mbar_init(smem_u32(&clc_full[s]), 1);
       mbar_init(smem_u32(&clc_empty[s]), kClcReaders);
+      mbar_init(smem_u32(&s_free[s]), kSoftmaxThreads);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -730,23 +735,118 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         item = read_next(it, false);
       }
     }
+  } else if (warp == 1 && kF8) {
+    // ------------------------- UMMA issuer, e4m3 inputs -------------------------
+    // P_X goes through shared memory, so QK_X(j+1) is issued as soon as the softmax has read
+    // S_X(j), and runs while the softmax computes P_X(j); PV_X(j) follows P_X(j).
+    if (lane == 0) {
+      const uint32_t idesc_qk = idesc_e4m3(BM, BN);
+      const uint32_t idesc_pv = idesc_e4m3(BM, D);
+      const uint32_t sP = smem_u32(smem + G::P_OFF);
+      uint32_t nqk[2] = {0u, 0u};  // QK_X issued
+      uint32_t npf[2] = {0u, 0u};  // P_X tiles consumed
+      // Issues QK_X from key slot kslot once the softmax has read the previous S_X.
+      auto issue_qk8 = [&](int X, int kslot) -> bool {
+        if (nqk[X] > 0 && !mbar_wait(smem_u32(&s_free[X]), (nqk[X] - 1) & 1, abort_flag,
+                                     &g_flash_status, TLLM_DEV_WAIT_TIMEOUT + SITE_SFREE))
+          return false;
+        tc_fence_after();
+        const uint32_t kbase = sK + kslot * G::TILE_BYTES;
+        const uint32_t qbase = sQ + X * G::TILE_BYTES;
+#pragma unroll
+        for (int k = 0; k < G::ROWB / 32; ++k)
+          umma_f8_ss(tmem_base + X * BN, kmajor_desc_g<G>(qbase, k), kmajor_desc_g<G>(kbase, k),
+                     idesc_qk, k != 0 ? 1u : 0u);
+        umma_commit(smem_u32(&s_full[X]));
+        ++nqk[X];
+        return true;
+      };
+      int item = static_cast<int>(blockIdx.x);
+      int g = 0, nq = 0;
+      bool ok = true;
+      for (int it = 0; ok && item >= 0; ++it) {
+        const PPItem w = pp_item<kVarlen>(a, item);
+        if (w.n_kv > 0) {
+          ok = mbar_wait(smem_u32(q_full), nq & 1, abort_flag, &g_flash_status,
+                         TLLM_DEV_WAIT_TIMEOUT + SITE_Q) &&
+               mbar_wait(smem_u32(&k_full[g & 1]), (g >> 1) & 1, abort_flag, &g_flash_status,
+                         TLLM_DEV_WAIT_TIMEOUT + SITE_KFULL);
+          ++nq;
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int X = 0; X < 2; ++X)
+            if (ok && w.nkv[X] > 0) ok = issue_qk8(X, g & 1);
+          if (!ok) break;
+          umma_commit(smem_u32(&k_empty[g & 1]));
+          if (w.n_kv == 1) umma_commit(smem_u32(q_empty));
+          for (int j = 0; j < w.n_kv && ok; ++j) {
+            const int gj = g + j;
+            const int s = gj & 1;
+            if (j + 1 < w.n_kv) {
+              if (!mbar_wait(smem_u32(&k_full[(gj + 1) & 1]), ((gj + 1) >> 1) & 1, abort_flag,
+                             &g_flash_status, TLLM_DEV_WAIT_TIMEOUT + SITE_KFULL)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+#pragma unroll
+              for (int X = 0; X < 2; ++X)
+                if (ok && j + 1 < w.nkv[X]) ok = issue_qk8(X, (gj + 1) & 1);
+              if (!ok) break;
+              umma_commit(smem_u32(&k_empty[(gj + 1) & 1]));
+              // The item's last QK has been issued: its Q tiles are free once it completes.
+              if (j == w.n_kv - 2) umma_commit(smem_u32(q_empty));
+            }
+            if (!mbar_wait(smem_u32(&v_full[s]), (gj >> 1) & 1, abort_flag, &g_flash_status,
+                           TLLM_DEV_WAIT_TIMEOUT + SITE_VFULL)) {
+              ok = false;
+              break;
+            }
+            const uint32_t vbase = sV + s * G::TILE_BYTES;
+#pragma unroll
+            for (int X = 0; X < 2; ++X) {
+              if (j >= w.nkv[X]) continue;
+              if (!mbar_wait(smem_u32(&p_full[X]), npf[X] & 1, abort_flag, &g_flash_status,
+                             TLLM_DEV_WAIT_TIMEOUT + SITE_PFULL)) {
+                ok = false;
+                break;
+              }
+              ++npf[X];
+              tc_fence_after();
+              const uint32_t pbase = sP + X * G::P_TILE_BYTES;
+              const uint32_t o_tmem = tmem_base + O_COL + X * BN;
+              // A = P_X (128 rows of 128 keys), B = V transposed (D rows of 128 keys); both
+              // one 128-byte span, 32 keys a step.
+#pragma unroll
+              for (int k = 0; k < BN / 32; ++k)
+                umma_f8_ss(o_tmem, make_sdesc(pbase + k * 32, 16, 1024, 2u),
+                           make_sdesc(vbase + k * 32, 16, 1024, 2u), idesc_pv,
+                           (j | k) != 0 ? 1u : 0u);
+              umma_commit(smem_u32(&o_done[X]));
+            }
+            if (!ok) break;
+            umma_commit(smem_u32(&v_empty[s]));
+          }
+          g += w.n_kv;
+        }
+        if (!ok || !kSteal) break;
+        item = read_next(it, false);
+        if (item >= -1) mbar_arrive(smem_u32(&clc_empty[it & 1]));
+      }
+    }
   } else if (warp == 1) {
     // ------------------------------ UMMA issuer -------------------------------
     if (lane == 0) {
-      const uint32_t idesc_qk = kF8 ? idesc_e4m3(BM, BN) : make_idesc_f16(BM, BN, kBF16, false, false);
-      const uint32_t idesc_pv = kF8 ? idesc_e4m3(BM, D) : make_idesc_f16(BM, D, kBF16, false, true);
+      const uint32_t idesc_qk = make_idesc_f16(BM, BN, kBF16, false, false);
+      const uint32_t idesc_pv = make_idesc_f16(BM, D, kBF16, false, true);
       auto issue_qk = [&](int X, int kslot) {
         const uint32_t kbase = sK + kslot * G::TILE_BYTES;
         const uint32_t qbase = sQ + X * G::TILE_BYTES;
 #pragma unroll
-        for (int k = 0; k < G::ROWB / 32; ++k) {
-          if constexpr (kF8)
-            umma_f8_ss(tmem_base + X * BN, kmajor_desc_g<G>(qbase, k), kmajor_desc_g<G>(kbase, k),
-                       idesc_qk, k != 0 ? 1u : 0u);
-          else
-            umma_f16_ss(tmem_base + X * BN, kmajor_desc<D>(qbase, k), kmajor_desc<D>(kbase, k),
-                        idesc_qk, k != 0 ? 1u : 0u);
-        }
+        for (int k = 0; k < D / 16; ++k)
+          umma_f16_ss(tmem_base + X * BN, kmajor_desc<D>(qbase, k), kmajor_desc<D>(kbase, k),
+                      idesc_qk, k != 0 ? 1u : 0u);
         umma_commit(smem_u32(&s_full[X]));
       };
       int item = static_cast<int>(blockIdx.x);
@@ -793,19 +893,11 @@ __global__ void __launch_bounds__(kPPThreads, 1)
               tc_fence_after();
               const uint32_t p_tmem = tmem_base + X * BN;
               const uint32_t o_tmem = tmem_base + O_COL + X * BN;
-              if constexpr (kF8) {
-                // B = V transposed: D rows of 128 keys (one 128-byte span); 32 keys a step.
 #pragma unroll
-                for (int k = 0; k < BN / 32; ++k)
-                  umma_f8_ts(o_tmem, p_tmem + k * 8, make_sdesc(vbase + k * 32, 16, 1024, 2u),
-                             idesc_pv, (j | k) != 0 ? 1u : 0u);
-              } else {
-#pragma unroll
-                for (int k = 0; k < BN / 16; ++k) {
-                  const uint64_t bdesc =
-                      make_sdesc(vbase + k * 16 * G::SWB, G::CHUNK_BYTES, 8 * G::SWB, G::LAYOUT);
-                  umma_f16_ts(o_tmem, p_tmem + k * 8, bdesc, idesc_pv, (j | k) != 0 ? 1u : 0u);
-                }
+              for (int k = 0; k < BN / 16; ++k) {
+                const uint64_t bdesc =
+                    make_sdesc(vbase + k * 16 * G::SWB, G::CHUNK_BYTES, 8 * G::SWB, G::LAYOUT);
+                umma_f16_ts(o_tmem, p_tmem + k * 8, bdesc, idesc_pv, (j | k) != 0 ? 1u : 0u);
               }
               if (j == w.nkv[X] - 1) {
                 umma_commit(smem_u32(&o_done[X]));
@@ -869,6 +961,11 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         // The whole S row in one TMEM round trip (four 32-column loads, one wait).
         uint32_t sr[BN];
         tmem_ld4x32(s_tm, sr);
+        if constexpr (kF8) {
+          // S_X(j) is in registers: QK_X(j+1) may overwrite it while P_X(j) is computed.
+          tc_fence_before();
+          mbar_arrive(smem_u32(&s_free[X]));
+        }
         if (need_mask) {
 #pragma unroll
           for (int t = 0; t < BN; ++t) {
@@ -897,35 +994,50 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           rescale = true;
         }
         const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
-        // P = 2^(s * scale - m), written over S's first 64 columns in packed pairs (S's values
-        // are all in registers by now). Exponent arguments and the row sum use packed fp32
-        // pairs (one instruction per pair).
         const uint64_t scale2 = f2_pack(a.scale_log2, a.scale_log2);
         const uint64_t negm2 = f2_pack(neg_m, neg_m);
         uint64_t ps2[4] = {0ull, 0ull, 0ull, 0ull};
+        if constexpr (kF8) {
+          // P = 2^(s * scale - m) as e4m3, four keys a word, kept in registers until PV_X(j-1)
+          // has finished with P_X's shared-memory tile and with O_X.
+          uint32_t pk[BN / 4];
 #pragma unroll
-        for (int hlf = 0; hlf < 2; ++hlf) {
-          if constexpr (kF8) {
-            // e4m3 P: keys 64*hlf .. +63 in 16 columns.
-            uint32_t pk[16];
+          for (int t = 0; t < BN; t += 4) {
+            float pv[4];
 #pragma unroll
-            for (int t = 0; t < 64; t += 4) {
-              float pv[4];
-#pragma unroll
-              for (int u = 0; u < 4; u += 2) {
-                const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sr[64 * hlf + t + u]),
-                                                   __uint_as_float(sr[64 * hlf + t + u + 1])),
-                                           scale2, negm2);
-                float x0, x1;
-                f2_unpack(x2, x0, x1);
-                pv[u] = ex2_approx(x0);
-                pv[u + 1] = ex2_approx(x1);
-                ps2[((t + u) >> 1) & 3] = f2_add(ps2[((t + u) >> 1) & 3], f2_pack(pv[u], pv[u + 1]));
-              }
-              pk[t >> 2] = pack4_e4m3(pv[0], pv[1], pv[2], pv[3]);
+            for (int u = 0; u < 4; u += 2) {
+              const uint64_t x2 = f2_fma(
+                  f2_pack(__uint_as_float(sr[t + u]), __uint_as_float(sr[t + u + 1])), scale2, negm2);
+              float x0, x1;
+              f2_unpack(x2, x0, x1);
+              pv[u] = ex2_approx(x0);
+              pv[u + 1] = ex2_approx(x1);
+              ps2[((t + u) >> 1) & 3] = f2_add(ps2[((t + u) >> 1) & 3], f2_pack(pv[u], pv[u + 1]));
             }
-            tmem_st16(s_tm + 16 * hlf, pk);
-          } else {
+            pk[t >> 2] = pack4_e4m3(pv[0], pv[1], pv[2], pv[3]);
+          }
+          if (j > 0) {
+            if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&o_done[X]), nod & 1, abort_flag,
+                                                   &g_flash_status, TLLM_DEV_WAIT_TIMEOUT + SITE_ODONE))) {
+              ok = false;
+              break;
+            }
+            ++nod;
+            tc_fence_after();
+          }
+          // Row `row` of P_X in the K-major 128-byte-swizzled layout: 16-byte unit u of the
+          // row at unit u ^ (row % 8) (eight consecutive rows fill all banks).
+          const uint32_t prow = smem_u32(smem + G::P_OFF + X * G::P_TILE_BYTES) + row * 128;
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            st_shared_v4(prow + ((u ^ (row & 7)) << 4), pk[4 * u], pk[4 * u + 1], pk[4 * u + 2],
+                         pk[4 * u + 3]);
+        } else {
+          // P = 2^(s * scale - m), written over S's first 64 columns in packed pairs (S's
+          // values are all in registers by now). Exponent arguments and the row sum use packed
+          // fp32 pairs (one instruction per pair).
+#pragma unroll
+          for (int hlf = 0; hlf < 2; ++hlf) {
             uint32_t pk[32];
 #pragma unroll
             for (int t = 0; t < 64; t += 2) {
@@ -949,8 +1061,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         f2_unpack(ps2[3], psg, psh);
         const float psum = ((psa + psb) + (psc + psd)) + ((pse + psf) + (psg + psh));
         l_run = l_run * alpha + psum;
-        // O_X is stable here: PV_X(j-1) was issued before QK_X(j), whose completion s_full
-        // signalled.
+        // O_X is stable here: 16-bit inputs issue PV_X(j-1) before QK_X(j), whose completion
+        // s_full signalled; e4m3 inputs waited for PV_X(j-1) above.
         if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
           for (int c = 0; c < D; c += OC) {
@@ -961,6 +1073,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
             tmem_st_cols(o_tm + c, r);
           }
         }
+        // P_X's shared-memory writes become visible to the tensor core (async proxy).
+        if constexpr (kF8) fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(smem_u32(&p_full[X]));
       }
