@@ -45,6 +45,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--chunks", type=int, default=1,
                     help="N>1 with --comm nccl: row chunks whose all-gather overlaps the next GEMM")
+    ap.add_argument("--e2e-chunks", type=int, default=8,
+                    help="column blocks of the 1-GPU end-to-end host pipeline")
     ap.add_argument("--comm", choices=["peers", "nccl"], default="peers",
                     help="N>1: peers = the GEMM epilogue stores into every rank's output over "
                          "NVLink; nccl = all_gather_into_tensor + permute")
@@ -679,14 +681,21 @@ def run_ours(args):
 
     if world > 1:
         hout = torch.empty((M, N), dtype=torch.float16).pin_memory()
+    else:
+        # One GPU: the public host-memory entry, which pipelines the weight upload, the kernel
+        # and the result download over column blocks on three streams.
+        from tritonllmcompiler_b200.ops.host_pipeline import SwigluHostPipeline
+        host_pipe = SwigluHostPipeline(M, n_loc, K, torch.float16, torch.device("cuda", local),
+                                       chunks=args.e2e_chunks)
 
     def e2e_step():
+        if world == 1:
+            host_pipe(hx, h1, h3, hout)
+            return
         dx.copy_(hx, non_blocking=True)
         d1.copy_(h1, non_blocking=True)
         d3.copy_(h3, non_blocking=True)
-        if world == 1:
-            out = T.swiglu(dx, d1, d3)
-        elif peers is not None:
+        if peers is not None:
             out = S.swiglu_column_sharded(dx, d1, d3, peers=peers)
         else:
             out = S.swiglu_column_sharded(dx, d1, d3, chunks=args.chunks, out=out_full)
@@ -700,13 +709,16 @@ def run_ours(args):
         e_ms = float(tt.item())
     e2e = {"value": flops / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
            "h2d_bytes_per_step": (hx.numel() + h1.numel() + h3.numel()) * 2,
-           "d2h_bytes_per_step": hout.numel() * 2, "ms_per_step": e_ms}
+           "d2h_bytes_per_step": hout.numel() * 2, "ms_per_step": e_ms,
+           "path": (f"ops.host_pipeline.SwigluHostPipeline, {len(host_pipe.blocks)} column blocks: "
+                    f"upload, kernel and download overlapped on three streams") if world == 1 else
+                   "H2D copies, sharded swiglu, D2H copy on one stream"}
 
     ops = None
     cpu = None
     if rank == 0 and world == 1:
         if not args.no_ops:
-            del dx, d1, d3
+            del dx, d1, d3, host_pipe
             torch.cuda.empty_cache()
             ops = extra_ops(torch, T, peaks)
         if not args.no_cpu:

@@ -188,6 +188,14 @@ TLLM_API int tllm_ipc_get_handle(const void *ptr, void *handle_out, uint64_t *of
 TLLM_API int tllm_ipc_open(const void *handle, uint64_t offset, void **ptr_out, void **base_out);
 TLLM_API int tllm_ipc_close(void *base);
 
+/* Asynchronous 2-D copy (height rows of width bytes, row pitches in bytes) between any two of
+ * host (pinned) and device memory on `stream`: one DMA request for a column block of a
+ * row-major matrix. Used by the host-memory pipelines of the Python package
+ * (ops/host_pipeline.py), which overlap the transfer of one block with the kernel on the
+ * previous one; no counterpart in the reference. */
+TLLM_API int tllm_copy2d_async(void *dst, size_t dpitch, const void *src, size_t spitch,
+                               size_t width, size_t height, void *stream);
+
 /*
  * Operators either side of decode (no counterpart in the reference, which only decodes from a
  * paged cache: python/triton_llm/ops/paged_attention.py:92-128). They use its cache layout:

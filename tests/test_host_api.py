@@ -60,3 +60,12 @@ def test_no_cpu_fallback_in_product_code():
             if f.endswith(".py"):
                 src = open(os.path.join(dirpath, f)).read()
                 assert "from oracle" not in src and "import oracle" not in src
+
+
+def test_host_pipeline_column_blocks():
+    from tritonllmcompiler_b200.ops.host_pipeline import _blocks
+    for n, c in [(14336, 8), (1000, 3), (128, 8), (100, 4), (14336, 1), (5000, 16)]:
+        b = _blocks(n, c)
+        assert b[0][0] == 0 and b[-1][1] == n
+        assert all(b0 < b1 for b0, b1 in b) and all(b[i][1] == b[i + 1][0] for i in range(len(b) - 1))
+        assert all(b0 % 128 == 0 for b0, _ in b) and len(b) <= max(c, 1)

@@ -60,6 +60,8 @@ SIGNATURES = {
     "tllm_ipc_open": (ctypes.c_int, [_vp, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p),
                                      ctypes.POINTER(ctypes.c_void_p)]),
     "tllm_ipc_close": (ctypes.c_int, [_vp]),
+    "tllm_copy2d_async": (ctypes.c_int, [_vp, ctypes.c_size_t, _vp, ctypes.c_size_t, ctypes.c_size_t,
+                                         ctypes.c_size_t, _vp]),
     "tllm_paged_kv_append": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64,

@@ -185,4 +185,16 @@ int tllm_ipc_close(void *base) {
   return tllm::cuda_status(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle");
 }
 
+int tllm_copy2d_async(void *dst, size_t dpitch, const void *src, size_t spitch, size_t width,
+                      size_t height, void *stream) {
+  tllm::clear_error();
+  if (width == 0 || height == 0) return TLLM_OK;
+  if (!dst || !src) return tllm::fail(TLLM_ERR_INVALID, "tllm_copy2d_async: null pointer");
+  if (dpitch < width || spitch < width)
+    return tllm::fail(TLLM_ERR_INVALID, "tllm_copy2d_async: pitch below the row width");
+  return tllm::cuda_status(cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, height,
+                                             cudaMemcpyDefault, static_cast<cudaStream_t>(stream)),
+                           "cudaMemcpy2DAsync");
+}
+
 }  // extern "C"
