@@ -265,15 +265,16 @@ def test_paged_int64_metadata_and_strided_q(cuda_device):
                                             (1, 2, 300, 32, True), (1, 2, 257, 16, False),
                                             (4, 64, 2048, 128, True), (2, 32, 1536, 64, False)])
 def test_flash_kernel_variants_agree(cuda_device, b, h, s, d, causal):
-    """The two-tile kernel (work stealing, the default), the single-tile kernel and the
-    two-tile kernel with one item per CTA agree; work stealing changes only which CTA computes
-    an item, so variants 0 and 2 match bit for bit."""
+    """The two-tile kernel (work stealing, the default), the single-tile kernel, the two-tile
+    kernel with one item per CTA and the two-tile kernel with P in shared memory agree; work
+    stealing changes only which CTA computes an item, and P holds the same values in TMEM or in
+    shared memory, so variants 0, 2 and 3 match bit for bit."""
     from tritonllmcompiler_b200 import _lib
 
     g = _gen(s + d)
     q, k, v = (torch.randn(b, h, s, d, generator=g).half().cuda() for _ in range(3))
     outs = []
-    for variant in (0, 1, 2):
+    for variant in (0, 1, 2, 3):
         o = torch.empty_like(q)
         _lib.check(_lib.load().tllm_flash_attn_fwd_variant(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), b, h, s, s, d,
@@ -283,4 +284,5 @@ def test_flash_kernel_variants_agree(cuda_device, b, h, s, d, causal):
     for o in outs[1:]:
         assert torch.allclose(outs[0].float(), o.float(), **G.tol(torch.float16))
     assert torch.equal(outs[0], outs[2])
+    assert torch.equal(outs[0], outs[3])
     assert _lib.debug_status() == 0

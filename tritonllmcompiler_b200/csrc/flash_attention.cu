@@ -437,9 +437,12 @@ constexpr int kGroupHeads = 8;
 
 // Shared memory of the two-tile kernel for head dim D and EB-byte inputs. A Q or K tile is
 // 128 rows of D * EB bytes in 128-byte-swizzled spans of SWB bytes; with 16-bit inputs a V
-// tile has the same shape, with e4m3 inputs it is V transposed (D rows of 128 keys, 128 B)
-// and each query tile also has a P tile in shared memory (128 rows of 128 e4m3 keys).
-template <int D, int EB = 2>
+// tile has the same shape, with e4m3 inputs it is V transposed (D rows of 128 keys, 128 B).
+// kSP (P through shared memory): each query tile also has a P tile (128 rows of 128 keys, in
+// the K-major layout of a 128-wide Q tile), and K and V tiles share one ring of NS slots,
+// filled and consumed in the order K0, K1, V0, K2, V1, ... (three slots keep the 16-bit
+// D = 128 kernel within 227 KB).
+template <int D, int EB = 2, bool kSP = false>
 struct GeoPP {
   static constexpr int ROWB = D * EB;
   static constexpr int SWB = ROWB >= 128 ? 128 : ROWB;
@@ -450,13 +453,15 @@ struct GeoPP {
   static constexpr uint32_t LAYOUT = SWB == 128 ? 2u : (SWB == 64 ? 4u : 6u);
   static_assert(EB == 2 || (D * BN == TILE_BYTES && (D == 64 || D == 128)),
                 "e4m3 tiles: head dim 64 or 128");
+  static constexpr int NS = (EB == 2 && D == 128) ? 3 : 4;
   static constexpr int Q_OFF = 0;                       // two Q tiles
-  static constexpr int K_OFF = Q_OFF + 2 * TILE_BYTES;  // two K slots
-  static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;  // two V slots
-  static constexpr int P_OFF = V_OFF + 2 * TILE_BYTES;  // e4m3: two P tiles
-  static constexpr int P_TILE_BYTES = BM * BN;
-  static constexpr int BAR_OFF = P_OFF + (EB == 1 ? 2 * P_TILE_BYTES : 0);
+  static constexpr int K_OFF = Q_OFF + 2 * TILE_BYTES;  // two K slots, or the kSP ring
+  static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;  // two V slots (not kSP)
+  static constexpr int P_TILE_BYTES = BM * BN * EB;
+  static constexpr int P_OFF = kSP ? K_OFF + NS * TILE_BYTES : V_OFF + 2 * TILE_BYTES;
+  static constexpr int BAR_OFF = P_OFF + (kSP ? 2 * P_TILE_BYTES : 0);
   static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+  static_assert(SMEM_BYTES <= 232448, "two-tile kernel: shared memory above the 227 KB limit");
 };
 
 enum : int { SITE_PFULL = 9, SITE_ODONE = 10, SITE_QEMPTY = 11, SITE_CLC = 12, SITE_SFREE = 13 };
@@ -583,14 +588,16 @@ __device__ __forceinline__ uint32_t pack4_e4m3(float p0, float p1, float p2, flo
 // K-major, and P goes through shared memory as e4m3 (16 KB per query tile): the softmax frees
 // S_X as soon as it has loaded it, so QK_X(j+1) runs on the tensor core while P_X(j) is being
 // computed, instead of after PV_X(j).
-template <typename T, typename TI, int D, bool kSteal, bool kVarlen>
+template <typename T, typename TI, int D, bool kSteal, bool kVarlen, bool kSP>
 __global__ void __launch_bounds__(kPPThreads, 1)
     flash_pp_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const Args a) {
   constexpr bool kF8 = std::is_same<TI, __nv_fp8_e4m3>::value;
-  static_assert(!kF8 || !kVarlen, "e4m3 inputs: dense batches only");
-  using G = GeoPP<D, kF8 ? 1 : 2>;
+  static_assert(!kF8 || (!kVarlen && kSP), "e4m3 inputs: dense batches, P in shared memory");
+  constexpr int EB = kF8 ? 1 : 2;
+  using G = GeoPP<D, EB, kSP>;
+  using PG = GeoPP<BN, EB>;  // a P tile has the layout of a Q tile with 128 columns
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr int OC = D < 32 ? D : 32;
   extern __shared__ uint8_t smem_raw[];
@@ -611,9 +618,12 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 20);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
   const uint32_t clc_resp = smem_u32(bars + 22);  // two 16-byte responses
-  // e4m3 only: S_X has been read into registers (the next QK_X may overwrite it); o_done then
-  // completes after every PV_X (P_X in shared memory and O_X may be reused).
+  // kSP: S_X has been read into registers (the next QK_X may overwrite it); o_done then
+  // completes after every PV_X (P_X in shared memory and O_X may be reused). The K/V ring uses
+  // k_full..v_empty as ring_full[4] and ring_empty[4].
   uint64_t *s_free = bars + 26;    // [2] per tile
+  uint64_t *ring_full = bars + 1;  // [NS]
+  uint64_t *ring_empty = bars + 5; // [NS]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -666,7 +676,72 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   };
   if (warp < kPPSoftmaxWarp0) {
   regs_dec<kPPRegsLow>();
-  if (warp == 0) {
+  if (warp == 0 && kSP) {
+    // ------------------------ TMA producer, one K/V ring ------------------------
+    if (lane == 0) {
+      int item = static_cast<int>(blockIdx.x);
+      int gr = 0;  // ring tiles loaded so far
+      int nq = 0;  // Q loads so far
+      bool ok = true;
+      // Loads key tile j (is_v false) or value tile j into the next ring slot.
+      auto load_kv = [&](const PPItem &w, bool is_v, int j) -> bool {
+        const int r = gr % G::NS;
+        if (!mbar_wait(smem_u32(&ring_empty[r]), ((gr / G::NS) & 1) ^ 1, abort_flag,
+                       &g_flash_status, TLLM_DEV_WAIT_TIMEOUT + (is_v ? SITE_VEMPTY : SITE_KEMPTY)))
+          return false;
+        const uint32_t fb = smem_u32(&ring_full[r]);
+        const uint32_t dst = sK + r * G::TILE_BYTES;
+        mbar_arrive_expect_tx(fb, G::TILE_BYTES);
+        if (kF8 && is_v) {
+          // One box of V transposed: 128 keys (x, a multiple of 128) of all D rows.
+          tma_load_4d(dst, &tm_v, fb, w.krow + j * BN, 0, w.hk, w.bc);
+        } else {
+#pragma unroll
+          for (int c = 0; c < G::CHUNKS; ++c)
+            tma_load_4d(dst + c * G::CHUNK_BYTES, is_v ? &tm_v : &tm_k, fb, c * G::CHUNK_ELEMS,
+                        w.krow + j * BN, w.hk, w.bc);
+        }
+        ++gr;
+        return true;
+      };
+      for (int it = 0; ok && item >= 0; ++it) {
+        const PPItem w = pp_item<kVarlen>(a, item);
+        if (w.n_kv > 0) {
+          // The previous item's last QK has read its Q tiles.
+          if (nq > 0 && !mbar_wait(smem_u32(q_empty), (nq - 1) & 1, abort_flag, &g_flash_status,
+                                   TLLM_DEV_WAIT_TIMEOUT + SITE_QEMPTY))
+            break;
+          const uint32_t qb = smem_u32(q_full);
+          mbar_arrive_expect_tx(qb, G::TILE_BYTES * ((w.nkv[0] > 0) + (w.nkv[1] > 0)));
+#pragma unroll
+          for (int X = 0; X < 2; ++X) {
+            if (w.nkv[X] == 0) continue;
+#pragma unroll
+            for (int c = 0; c < G::CHUNKS; ++c)
+              tma_load_4d(sQ + X * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_q, qb,
+                          c * G::CHUNK_ELEMS, w.qrow + w.q0 + X * BM, w.h, w.bc);
+          }
+          ++nq;
+          // The order the UMMA warp consumes them in: K0, then K(j+1) before V(j).
+          ok = load_kv(w, false, 0);
+          for (int j = 0; ok && j < w.n_kv; ++j) {
+            if (j + 1 < w.n_kv) ok = load_kv(w, false, j + 1);
+            if (ok) ok = load_kv(w, true, j);
+          }
+        }
+        if (!ok || !kSteal) break;
+        // Claim the next item while this one's last tiles are in flight.
+        const int slot = it & 1;
+        if (it >= 2 && !mbar_wait(smem_u32(&clc_empty[slot]), ((it >> 1) - 1) & 1, abort_flag,
+                                  &g_flash_status, TLLM_DEV_WAIT_TIMEOUT + SITE_CLC))
+          break;
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(smem_u32(&clc_full[slot]), 16);
+        clc_try_cancel(clc_resp + 16 * slot, smem_u32(&clc_full[slot]));
+        item = read_next(it, false);
+      }
+    }
+  } else if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
     if (lane == 0) {
       int item = static_cast<int>(blockIdx.x);
@@ -712,15 +787,10 @@ __global__ void __launch_bounds__(kPPThreads, 1)
             }
             const uint32_t vb = smem_u32(&v_full[s]);
             mbar_arrive_expect_tx(vb, G::TILE_BYTES);
-            if constexpr (kF8) {
-              // One box of V transposed: 128 keys (x, a multiple of 128) of all D rows.
-              tma_load_4d(sV + s * G::TILE_BYTES, &tm_v, vb, j * BN, 0, w.hk, w.bc);
-            } else {
 #pragma unroll
-              for (int c = 0; c < G::CHUNKS; ++c)
-                tma_load_4d(sV + s * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_v, vb,
-                            c * G::CHUNK_ELEMS, w.krow + j * BN, w.hk, w.bc);
-            }
+            for (int c = 0; c < G::CHUNKS; ++c)
+              tma_load_4d(sV + s * G::TILE_BYTES + c * G::CHUNK_BYTES, &tm_v, vb,
+                          c * G::CHUNK_ELEMS, w.krow + j * BN, w.hk, w.bc);
           }
         }
         if (!ok || !kSteal) break;
@@ -735,75 +805,81 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         item = read_next(it, false);
       }
     }
-  } else if (warp == 1 && kF8) {
-    // ------------------------- UMMA issuer, e4m3 inputs -------------------------
-    // P_X goes through shared memory, so QK_X(j+1) is issued as soon as the softmax has read
-    // S_X(j), and runs while the softmax computes P_X(j); PV_X(j) follows P_X(j).
+  } else if (warp == 1 && kSP) {
+    // ------------------------- UMMA issuer, P in shared memory ------------------
+    // QK_X(j+1) is issued as soon as the softmax has read S_X(j) and runs while the softmax
+    // computes P_X(j); PV_X(j) follows P_X(j). Ring tiles are consumed in load order.
     if (lane == 0) {
-      const uint32_t idesc_qk = idesc_e4m3(BM, BN);
-      const uint32_t idesc_pv = idesc_e4m3(BM, D);
+      const uint32_t idesc_qk = kF8 ? idesc_e4m3(BM, BN) : make_idesc_f16(BM, BN, kBF16, false, false);
+      // 16-bit: B = V [keys, D] MN-major; e4m3: B = V transposed [D, keys] K-major.
+      const uint32_t idesc_pv = kF8 ? idesc_e4m3(BM, D) : make_idesc_f16(BM, D, kBF16, false, true);
       const uint32_t sP = smem_u32(smem + G::P_OFF);
       uint32_t nqk[2] = {0u, 0u};  // QK_X issued
       uint32_t npf[2] = {0u, 0u};  // P_X tiles consumed
-      // Issues QK_X from key slot kslot once the softmax has read the previous S_X.
-      auto issue_qk8 = [&](int X, int kslot) -> bool {
+      int gc = 0;                  // ring tiles consumed
+      auto ring_acquire = [&](int site, uint32_t &base) -> bool {
+        const int r = gc % G::NS;
+        if (!mbar_wait(smem_u32(&ring_full[r]), (gc / G::NS) & 1, abort_flag, &g_flash_status,
+                       TLLM_DEV_WAIT_TIMEOUT + site))
+          return false;
+        tc_fence_after();
+        base = sK + r * G::TILE_BYTES;
+        return true;
+      };
+      // The slot is free once the MMAs issued so far (those reading it) have completed.
+      auto ring_release = [&]() {
+        umma_commit(smem_u32(&ring_empty[gc % G::NS]));
+        ++gc;
+      };
+      // Issues QK_X from the key tile at kbase once the softmax has read the previous S_X.
+      auto issue_qk = [&](int X, uint32_t kbase) -> bool {
         if (nqk[X] > 0 && !mbar_wait(smem_u32(&s_free[X]), (nqk[X] - 1) & 1, abort_flag,
                                      &g_flash_status, TLLM_DEV_WAIT_TIMEOUT + SITE_SFREE))
           return false;
         tc_fence_after();
-        const uint32_t kbase = sK + kslot * G::TILE_BYTES;
         const uint32_t qbase = sQ + X * G::TILE_BYTES;
 #pragma unroll
-        for (int k = 0; k < G::ROWB / 32; ++k)
-          umma_f8_ss(tmem_base + X * BN, kmajor_desc_g<G>(qbase, k), kmajor_desc_g<G>(kbase, k),
-                     idesc_qk, k != 0 ? 1u : 0u);
+        for (int k = 0; k < G::ROWB / 32; ++k) {
+          if constexpr (kF8)
+            umma_f8_ss(tmem_base + X * BN, kmajor_desc_g<G>(qbase, k), kmajor_desc_g<G>(kbase, k),
+                       idesc_qk, k != 0 ? 1u : 0u);
+          else
+            umma_f16_ss(tmem_base + X * BN, kmajor_desc_g<G>(qbase, k), kmajor_desc_g<G>(kbase, k),
+                        idesc_qk, k != 0 ? 1u : 0u);
+        }
         umma_commit(smem_u32(&s_full[X]));
         ++nqk[X];
         return true;
       };
       int item = static_cast<int>(blockIdx.x);
-      int g = 0, nq = 0;
+      int nq = 0;
       bool ok = true;
       for (int it = 0; ok && item >= 0; ++it) {
         const PPItem w = pp_item<kVarlen>(a, item);
         if (w.n_kv > 0) {
           ok = mbar_wait(smem_u32(q_full), nq & 1, abort_flag, &g_flash_status,
-                         TLLM_DEV_WAIT_TIMEOUT + SITE_Q) &&
-               mbar_wait(smem_u32(&k_full[g & 1]), (g >> 1) & 1, abort_flag, &g_flash_status,
-                         TLLM_DEV_WAIT_TIMEOUT + SITE_KFULL);
+                         TLLM_DEV_WAIT_TIMEOUT + SITE_Q);
           ++nq;
-          if (!ok) break;
-          tc_fence_after();
+          uint32_t kbase = 0, vbase = 0;
+          if (!ok || !(ok = ring_acquire(SITE_KFULL, kbase))) break;
 #pragma unroll
           for (int X = 0; X < 2; ++X)
-            if (ok && w.nkv[X] > 0) ok = issue_qk8(X, g & 1);
+            if (ok && w.nkv[X] > 0) ok = issue_qk(X, kbase);
           if (!ok) break;
-          umma_commit(smem_u32(&k_empty[g & 1]));
+          ring_release();
           if (w.n_kv == 1) umma_commit(smem_u32(q_empty));
           for (int j = 0; j < w.n_kv && ok; ++j) {
-            const int gj = g + j;
-            const int s = gj & 1;
             if (j + 1 < w.n_kv) {
-              if (!mbar_wait(smem_u32(&k_full[(gj + 1) & 1]), ((gj + 1) >> 1) & 1, abort_flag,
-                             &g_flash_status, TLLM_DEV_WAIT_TIMEOUT + SITE_KFULL)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
+              if (!(ok = ring_acquire(SITE_KFULL, kbase))) break;
 #pragma unroll
               for (int X = 0; X < 2; ++X)
-                if (ok && j + 1 < w.nkv[X]) ok = issue_qk8(X, (gj + 1) & 1);
+                if (ok && j + 1 < w.nkv[X]) ok = issue_qk(X, kbase);
               if (!ok) break;
-              umma_commit(smem_u32(&k_empty[(gj + 1) & 1]));
+              ring_release();
               // The item's last QK has been issued: its Q tiles are free once it completes.
               if (j == w.n_kv - 2) umma_commit(smem_u32(q_empty));
             }
-            if (!mbar_wait(smem_u32(&v_full[s]), (gj >> 1) & 1, abort_flag, &g_flash_status,
-                           TLLM_DEV_WAIT_TIMEOUT + SITE_VFULL)) {
-              ok = false;
-              break;
-            }
-            const uint32_t vbase = sV + s * G::TILE_BYTES;
+            if (!(ok = ring_acquire(SITE_VFULL, vbase))) break;
 #pragma unroll
             for (int X = 0; X < 2; ++X) {
               if (j >= w.nkv[X]) continue;
@@ -816,19 +892,25 @@ __global__ void __launch_bounds__(kPPThreads, 1)
               tc_fence_after();
               const uint32_t pbase = sP + X * G::P_TILE_BYTES;
               const uint32_t o_tmem = tmem_base + O_COL + X * BN;
-              // A = P_X (128 rows of 128 keys), B = V transposed (D rows of 128 keys); both
-              // one 128-byte span, 32 keys a step.
+              if constexpr (kF8) {
+                // A = P_X, B = V transposed (D rows of 128 keys); 32 keys a step.
 #pragma unroll
-              for (int k = 0; k < BN / 32; ++k)
-                umma_f8_ss(o_tmem, make_sdesc(pbase + k * 32, 16, 1024, 2u),
-                           make_sdesc(vbase + k * 32, 16, 1024, 2u), idesc_pv,
-                           (j | k) != 0 ? 1u : 0u);
+                for (int k = 0; k < BN / 32; ++k)
+                  umma_f8_ss(o_tmem, kmajor_desc_g<PG>(pbase, k),
+                             make_sdesc(vbase + k * 32, 16, 1024, 2u), idesc_pv, (j | k) != 0 ? 1u : 0u);
+              } else {
+                // A = P_X, B = V (keys x D, MN-major); 16 keys a step.
+#pragma unroll
+                for (int k = 0; k < BN / 16; ++k)
+                  umma_f16_ss(o_tmem, kmajor_desc_g<PG>(pbase, k),
+                              make_sdesc(vbase + k * 16 * G::SWB, G::CHUNK_BYTES, 8 * G::SWB, G::LAYOUT),
+                              idesc_pv, (j | k) != 0 ? 1u : 0u);
+              }
               umma_commit(smem_u32(&o_done[X]));
             }
             if (!ok) break;
-            umma_commit(smem_u32(&v_empty[s]));
+            ring_release();
           }
-          g += w.n_kv;
         }
         if (!ok || !kSteal) break;
         item = read_next(it, false);
@@ -961,7 +1043,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         // The whole S row in one TMEM round trip (four 32-column loads, one wait).
         uint32_t sr[BN];
         tmem_ld4x32(s_tm, sr);
-        if constexpr (kF8) {
+        if constexpr (kSP) {
           // S_X(j) is in registers: QK_X(j+1) may overwrite it while P_X(j) is computed.
           tc_fence_before();
           mbar_arrive(smem_u32(&s_free[X]));
@@ -997,24 +1079,40 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         const uint64_t scale2 = f2_pack(a.scale_log2, a.scale_log2);
         const uint64_t negm2 = f2_pack(neg_m, neg_m);
         uint64_t ps2[4] = {0ull, 0ull, 0ull, 0ull};
-        if constexpr (kF8) {
-          // P = 2^(s * scale - m) as e4m3, four keys a word, kept in registers until PV_X(j-1)
-          // has finished with P_X's shared-memory tile and with O_X.
-          uint32_t pk[BN / 4];
+        if constexpr (kSP) {
+          // P = 2^(s * scale - m) in the input precision (e4m3: four keys a word; 16-bit: two),
+          // kept in registers until PV_X(j-1) has finished with P_X's shared-memory tile and
+          // with O_X. Exponent arguments and the row sum use packed fp32 pairs.
+          constexpr int PW = BN * EB / 4;  // 32-bit words of a P row
+          uint32_t pk[PW];
+          if constexpr (kF8) {
 #pragma unroll
-          for (int t = 0; t < BN; t += 4) {
-            float pv[4];
+            for (int t = 0; t < BN; t += 4) {
+              float pv[4];
 #pragma unroll
-            for (int u = 0; u < 4; u += 2) {
+              for (int u = 0; u < 4; u += 2) {
+                const uint64_t x2 = f2_fma(
+                    f2_pack(__uint_as_float(sr[t + u]), __uint_as_float(sr[t + u + 1])), scale2, negm2);
+                float x0, x1;
+                f2_unpack(x2, x0, x1);
+                pv[u] = ex2_approx(x0);
+                pv[u + 1] = ex2_approx(x1);
+                ps2[((t + u) >> 1) & 3] = f2_add(ps2[((t + u) >> 1) & 3], f2_pack(pv[u], pv[u + 1]));
+              }
+              pk[t >> 2] = pack4_e4m3(pv[0], pv[1], pv[2], pv[3]);
+            }
+          } else {
+#pragma unroll
+            for (int t = 0; t < BN; t += 2) {
               const uint64_t x2 = f2_fma(
-                  f2_pack(__uint_as_float(sr[t + u]), __uint_as_float(sr[t + u + 1])), scale2, negm2);
+                  f2_pack(__uint_as_float(sr[t]), __uint_as_float(sr[t + 1])), scale2, negm2);
               float x0, x1;
               f2_unpack(x2, x0, x1);
-              pv[u] = ex2_approx(x0);
-              pv[u + 1] = ex2_approx(x1);
-              ps2[((t + u) >> 1) & 3] = f2_add(ps2[((t + u) >> 1) & 3], f2_pack(pv[u], pv[u + 1]));
+              const float p0 = ex2_approx(x0);
+              const float p1 = ex2_approx(x1);
+              ps2[(t >> 1) & 3] = f2_add(ps2[(t >> 1) & 3], f2_pack(p0, p1));
+              pk[t >> 1] = Pack2<T>::pack(p0, p1);
             }
-            pk[t >> 2] = pack4_e4m3(pv[0], pv[1], pv[2], pv[3]);
           }
           if (j > 0) {
             if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&o_done[X]), nod & 1, abort_flag,
@@ -1025,13 +1123,13 @@ __global__ void __launch_bounds__(kPPThreads, 1)
             ++nod;
             tc_fence_after();
           }
-          // Row `row` of P_X in the K-major 128-byte-swizzled layout: 16-byte unit u of the
-          // row at unit u ^ (row % 8) (eight consecutive rows fill all banks).
+          // Row `row` of P_X in the K-major 128-byte-swizzled layout: 16-byte unit u of a
+          // 128-byte span at unit u ^ (row % 8) (eight consecutive rows fill all banks).
           const uint32_t prow = smem_u32(smem + G::P_OFF + X * G::P_TILE_BYTES) + row * 128;
 #pragma unroll
-          for (int u = 0; u < 8; ++u)
-            st_shared_v4(prow + ((u ^ (row & 7)) << 4), pk[4 * u], pk[4 * u + 1], pk[4 * u + 2],
-                         pk[4 * u + 3]);
+          for (int u = 0; u < PW / 4; ++u)
+            st_shared_v4(prow + (u >> 3) * PG::CHUNK_BYTES + (((u & 7) ^ (row & 7)) << 4),
+                         pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
         } else {
           // P = 2^(s * scale - m), written over S's first 64 columns in packed pairs (S's
           // values are all in registers by now). Exponent arguments and the row sum use packed
@@ -1061,8 +1159,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         f2_unpack(ps2[3], psg, psh);
         const float psum = ((psa + psb) + (psc + psd)) + ((pse + psf) + (psg + psh));
         l_run = l_run * alpha + psum;
-        // O_X is stable here: 16-bit inputs issue PV_X(j-1) before QK_X(j), whose completion
-        // s_full signalled; e4m3 inputs waited for PV_X(j-1) above.
+        // O_X is stable here: with P in TMEM, PV_X(j-1) was issued before QK_X(j), whose
+        // completion s_full signalled; with P in shared memory it was waited for above.
         if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
           for (int c = 0; c < D; c += OC) {
@@ -1074,7 +1172,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           }
         }
         // P_X's shared-memory writes become visible to the tensor core (async proxy).
-        if constexpr (kF8) fence_proxy_async_smem();
+        if constexpr (kSP) fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(smem_u32(&p_full[X]));
       }
@@ -1145,6 +1243,7 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 constexpr int kVariantPingPong = 0;
 constexpr int kVariantSingleTile = 1;
 constexpr int kVariantPingPongOneItem = 2;
+constexpr int kVariantSmemP = 3;  // P through shared memory, one K/V ring
 
 // Packed variable-length batch: sequence b's rows are [cu_q[b], cu_q[b+1]) of q/o (total_q
 // rows) and [cu_k[b], cu_k[b+1]) of k/v (total_k rows, Hkv heads).
@@ -1255,11 +1354,14 @@ int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, in
     kern<<<grid, kThreads, G::SMEM_BYTES, st>>>(mq, mk, mv, a);
     return cuda_status(cudaGetLastError(), "flash launch");
   }
-  using GP = GeoPP<D>;
-  auto kern = vl ? flash_pp_kernel<T, T, D, true, true>
-                : (variant == kVariantPingPongOneItem ? flash_pp_kernel<T, T, D, false, false>
-                                                      : flash_pp_kernel<T, T, D, true, false>);
   const unsigned grid = static_cast<unsigned>(B * H * ((a.n_qtiles + 1) / 2));
+  if (variant == kVariantSmemP && !vl)
+    return launch_pp<GeoPP<D, 2, true>>(flash_pp_kernel<T, T, D, true, false, true>, grid, mq, mk,
+                                        mv, a, st);
+  using GP = GeoPP<D>;
+  auto kern = vl ? flash_pp_kernel<T, T, D, true, true, false>
+                : (variant == kVariantPingPongOneItem ? flash_pp_kernel<T, T, D, false, false, false>
+                                                      : flash_pp_kernel<T, T, D, true, false, false>);
   return launch_pp<GP>(kern, grid, mq, mk, mv, a, st);
 }
 
@@ -1270,7 +1372,7 @@ int launch_fp8(const void *q, const void *k, const void *vt, void *o, int64_t B,
                int64_t Sq, int64_t Sk, const int64_t *sq, const int64_t *sk, const int64_t *svt,
                const int64_t *so, float sm_scale, float scale_q, float scale_k, float scale_v,
                int causal, cudaStream_t st) {
-  using GP = GeoPP<D, 1>;
+  using GP = GeoPP<D, 1, true>;
   const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const CUtensorMapSwizzle sw = GP::SWB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   const uint32_t box[4] = {static_cast<uint32_t>(GP::SWB), static_cast<uint32_t>(BM), 1, 1};
@@ -1316,7 +1418,7 @@ int launch_fp8(const void *q, const void *k, const void *vt, void *o, int64_t B,
   a.out_scale = scale_v;
   set_groups(a, B, H, Sk, D, causal);
   const unsigned grid = static_cast<unsigned>(B * H * ((a.n_qtiles + 1) / 2));
-  return launch_pp<GP>(flash_pp_kernel<T, __nv_fp8_e4m3, D, true, false>, grid, mq, mk, mv, a, st);
+  return launch_pp<GP>(flash_pp_kernel<T, __nv_fp8_e4m3, D, true, false, true>, grid, mq, mk, mv, a, st);
 }
 
 template <typename T>
@@ -1351,7 +1453,7 @@ int entry(const void *q, const void *k, const void *v, void *o, int64_t B, int64
   TLLM_CHECK_ARG(dtype == TLLM_DTYPE_F16 || dtype == TLLM_DTYPE_BF16,
                  "flash_attention: unsupported dtype %d", dtype);
   TLLM_CHECK_ARG(variant == kVariantPingPong || variant == kVariantSingleTile ||
-                     variant == kVariantPingPongOneItem,
+                     variant == kVariantPingPongOneItem || variant == kVariantSmemP,
                  "flash_attention: unknown kernel variant %d", variant);
   TLLM_CHECK_ARG(sq && sk && sv && so, "flash_attention: null stride array");
   if (B == 0 || H == 0 || Sq == 0) return TLLM_OK;
