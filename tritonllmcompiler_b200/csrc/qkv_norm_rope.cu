@@ -150,8 +150,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sb = sa + A_BYTES;
           const int k0 = kb * BK;
           tma_load_2d(sa, &tm_x, fb, k0, m0);
-#pragma unroll
-          for (int c = 0; c < 4; ++c) tma_load_2d(sb + c * B_CHUNK_BYTES, &tm_w, fb, n0 + 64 * c, k0);
+          // All four 64-column chunks of the [BK x 256] weight tile in one box.
+          tma_load_3d(sb, &tm_w, fb, 0, k0, n0 >> 6);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -316,10 +316,13 @@ int launch(const void *x, const void *w, void *out, const Geom &g0, int64_t lda,
     if (rc) return rc;
   }
   {
-    const uint64_t dims[2] = {static_cast<uint64_t>(g0.N), static_cast<uint64_t>(g0.K)};
-    const uint64_t str[1] = {static_cast<uint64_t>(ldw) * 2};
-    const uint32_t box[2] = {64, BK};
-    int rc = encode_tiled(&mw, dt, 2, const_cast<void *>(w), dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    // 3-D view {64 columns, K, N / 64} of w (N is a multiple of the 128-wide head): the
+    // outer dimension steps 64 columns, so one box {64, BK, 4} lands the tile's four
+    // 128-byte-swizzled column chunks B_CHUNK_BYTES apart, as the UMMA descriptor expects.
+    const uint64_t dims[3] = {64, static_cast<uint64_t>(g0.K), static_cast<uint64_t>(g0.N / 64)};
+    const uint64_t str[2] = {static_cast<uint64_t>(ldw) * 2, 128};
+    const uint32_t box[3] = {64, BK, 4};
+    int rc = encode_tiled(&mw, dt, 3, const_cast<void *>(w), dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
   Geom g = g0;

@@ -6,7 +6,10 @@
 //
 // B200 design (persistent, warp-specialised, one CTA per SM):
 //   warp 0      TMA producer: per K-step one x tile [128 x 64] (K-major, 128B swizzle) and
-//               the matching w1 and w3 tiles [64 x 128] (N-major) into a 4-stage ring.
+//               the matching w1 and w3 tiles [64 x 128] (N-major) into a 4-stage ring; when N
+//               is a multiple of 128 the weights are read through 3-D maps {64 columns, K,
+//               N / 64} whose outer dimension steps 64 columns, so a whole [64 x 128] tile
+//               (two 128-byte-swizzled column chunks) is one TMA box (3 boxes a stage, not 5).
 //   warp 1      allocates 512 TMEM columns, then one lane issues tcgen05.mma: the w1 and w3
 //               tiles sit side by side in shared memory as ONE N=256 operand, so a single
 //               128x256x16 UMMA per k16 step computes [x@w1 | x@w3] into adjacent TMEM
@@ -72,6 +75,7 @@ struct Geom {
   int tiles_m, tiles_n, k_blocks;
   int64_t ldo;
   int vec_store;  // 16-byte stores allowed (ldo % 8 == 0 and every destination aligned)
+  int w3d;        // weight maps are 3-D {64 columns, K, N / 64}: one box per 128-column tile
   // Column-sharded mode (ndst > 0): each output tile is written at column offset col_off
   // of every destination (this rank's [M, N_total] buffer and its peers', over NVLink)
   // instead of to `out`.
@@ -185,10 +189,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sb = sa + A_BYTES;
           const int k0 = kb * BK;
           tma_load_2d(sa, &tm_x, fb, k0, m0);
-          tma_load_2d(sb + 0 * B_CHUNK_BYTES, &tm_w1, fb, n0, k0);
-          tma_load_2d(sb + 1 * B_CHUNK_BYTES, &tm_w1, fb, n0 + 64, k0);
-          tma_load_2d(sb + 2 * B_CHUNK_BYTES, &tm_w3, fb, n0, k0);
-          tma_load_2d(sb + 3 * B_CHUNK_BYTES, &tm_w3, fb, n0 + 64, k0);
+          if (g.w3d) {
+            tma_load_3d(sb + 0 * B_CHUNK_BYTES, &tm_w1, fb, 0, k0, n0 >> 6);
+            tma_load_3d(sb + 2 * B_CHUNK_BYTES, &tm_w3, fb, 0, k0, n0 >> 6);
+          } else {
+            tma_load_2d(sb + 0 * B_CHUNK_BYTES, &tm_w1, fb, n0, k0);
+            tma_load_2d(sb + 1 * B_CHUNK_BYTES, &tm_w1, fb, n0 + 64, k0);
+            tma_load_2d(sb + 2 * B_CHUNK_BYTES, &tm_w3, fb, n0, k0);
+            tma_load_2d(sb + 3 * B_CHUNK_BYTES, &tm_w3, fb, n0 + 64, k0);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -394,7 +403,19 @@ int launch(const void *x, const void *w1, const void *w3, void *out, int64_t M, 
                           CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
-  {
+  const bool w3d = N % 128 == 0;
+  if (w3d) {
+    const uint64_t dims[3] = {64, static_cast<uint64_t>(K), static_cast<uint64_t>(N / 64)};
+    const uint32_t box[3] = {64, BK, 2};
+    const uint64_t s1[2] = {static_cast<uint64_t>(ldb1) * 2, 128};
+    int rc = encode_tiled(&m1, dt, 3, const_cast<void *>(w1), dims, s1, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    const uint64_t s3[2] = {static_cast<uint64_t>(ldb3) * 2, 128};
+    rc = encode_tiled(&m3, dt, 3, const_cast<void *>(w3), dims, s3, box,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  } else {
     const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(K)};
     const uint32_t box[2] = {64, BK};
     const uint64_t s1[1] = {static_cast<uint64_t>(ldb1) * 2};
@@ -414,6 +435,7 @@ int launch(const void *x, const void *w1, const void *w3, void *out, int64_t M, 
   g.tiles_n = static_cast<int>((N + BN - 1) / BN);
   g.k_blocks = static_cast<int>((K + BK - 1) / BK);
   g.ldo = ldo;
+  g.w3d = w3d ? 1 : 0;
   g.ndst = ndst;
   g.col_off = col_off;
   bool dst_aligned = true;
