@@ -670,7 +670,7 @@ def run_ours(args):
     k_ms = sum(kt) / len(kt)
     k_flops = 4.0 * M * K * n_loc
     achieved = k_flops / (k_ms * 1e-3) / 1e12
-    traffic = profile_traffic("swiglu_tc_kernel_m4096_k4096_n14336_fp16.md") if world == 1 else None
+    traffic = profile_traffic("swiglu_pair_kernel_m4096_k4096_n14336_fp16.md") if world == 1 else None
 
     # End to end through the public API with pinned host buffers (H2D inputs, D2H result).
     hx = x.cpu().pin_memory()
@@ -742,7 +742,9 @@ def run_ours(args):
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_source": f"{peak_src} bf16_tflops (dense, burst)",
-                         "kernel_ms": k_ms, "kernel": "swiglu_tc_kernel"},
+                         "kernel_ms": k_ms,
+                         "kernel": ("swiglu_pair_kernel" if world == 1 or args.comm != "peers"
+                                    else "swiglu_tc_kernel (column-sharded, peer stores)")},
             "e2e": e2e,
             "gpu_launches": args.steps,
             "clocks": clk.summary(),

@@ -307,6 +307,14 @@ TLLM_API int tllm_flash_attn_bwd(const void *q, const void *k, const void *v, co
                                  const int64_t *sdv, float sm_scale, int causal, int dtype,
                                  void *stream);
 
+/* Same as tllm_swiglu with an explicit kernel choice, for cross-checking: 0 = automatic (the
+ * CTA-pair kernel when M >= 256 and N % 128 == 0), 1 = one CTA per 128 x 128 output tile,
+ * 2 = the CTA-pair kernel (two CTAs on two SMs share 256 x 128 output tiles through
+ * tcgen05.mma.cta_group::2; N % 128 == 0). M, N, K > 0. */
+TLLM_API int tllm_swiglu_variant(const void *x, const void *w1, const void *w3, void *out,
+                                 int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb1,
+                                 int64_t ldb3, int64_t ldo, int dtype, int variant, void *stream);
+
 /*
  * FP8 SwiGLU: out = silu(scale_x*scale_w1 * x@w1) * (scale_x*scale_w3 * x@w3) with e4m3 inputs
  * and per-tensor scales, fp32 accumulation, fp16/bf16 output. An extension of tllm_swiglu

@@ -99,6 +99,29 @@ def test_swiglu_random(cuda_device, m, n, k, dt):
     _assert_close(out, O.swiglu(_f32(x), _f32(w1), _f32(w3), dtype=dt))
 
 
+@pytest.mark.parametrize("m,n,k,dt", [(256, 128, 64, "fp16"), (300, 256, 1000, "bf16"),
+                                      (1000, 640, 520, "fp16"), (4096, 1024, 4096, "fp16")])
+def test_swiglu_kernel_variants_agree(cuda_device, m, n, k, dt):
+    """The CTA-pair kernel (tcgen05.mma.cta_group::2, two SMs per 256 x 128 tile) and the
+    one-CTA kernel accumulate every output element in the same K order: bit-identical."""
+    from tritonllmcompiler_b200 import _lib
+
+    g = _gen(m + n + k)
+    x = torch.randn(m, k, generator=g).to(_dt(dt)).cuda()
+    w1 = (torch.randn(k, n, generator=g) / math.sqrt(k)).to(_dt(dt)).cuda()
+    w3 = (torch.randn(k, n, generator=g) / math.sqrt(k)).to(_dt(dt)).cuda()
+    outs = []
+    for variant in (1, 2):
+        o = torch.empty(m, n, dtype=x.dtype, device="cuda")
+        _lib.check(_lib.load().tllm_swiglu_variant(
+            x.data_ptr(), w1.data_ptr(), w3.data_ptr(), o.data_ptr(), m, n, k, k, n, n, n,
+            _lib.DTYPE_CODES[x.dtype], variant, torch.cuda.current_stream().cuda_stream))
+        outs.append(o)
+    assert torch.equal(outs[0], outs[1])
+    _assert_close(outs[1], O.swiglu(_f32(x.cpu()), _f32(w1.cpu()), _f32(w3.cpu()), dtype=dt))
+    assert _lib.debug_status() == 0
+
+
 def test_swiglu_strided_inputs(cuda_device):
     g = _gen(21)
     big = torch.randn(200, 264, generator=g).half()

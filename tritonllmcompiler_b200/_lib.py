@@ -113,6 +113,10 @@ SIGNATURES = {
         [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
          _i64, _i64, _i64, ctypes.c_float, ctypes.c_int, _vp],
     ),
+    "tllm_swiglu_variant": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_int, ctypes.c_int, _vp],
+    ),
     "tllm_swiglu": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_int, _vp],

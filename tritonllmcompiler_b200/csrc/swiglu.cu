@@ -17,6 +17,8 @@
 //   warps 2-5   epilogue: tcgen05.ld the two fp32 accumulators of a row, silu(g)*u in fp32,
 //               one store in the I/O dtype. The accumulator is double-buffered in TMEM
 //               (2 x 256 columns) so the epilogue of tile i overlaps the main loop of i+1.
+// From M >= 256 (N a multiple of 128) swiglu_pair_kernel below runs instead: two CTAs on two
+// SMs share each 256 x 128 output tile through tcgen05.mma.cta_group::2.
 // Every CTA loads its own tiles; every mbarrier wait is bounded.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -339,6 +341,260 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// =======================================================================================
+// CTA-pair kernel (tcgen05.mma.cta_group::2): a cluster of two CTAs on two SMs computes a
+// 256 x 128 output tile. CTA r loads its own 128 rows of x and one weight tile (r = 0: w1,
+// r = 1: w3), [64 x 128] each, and the pair's leader (r = 0) issues 256 x 256 x 16 UMMAs
+// whose A rows come from both CTAs' x tiles and whose B columns are the two weight tiles, so
+// each CTA's TMEM receives its 128 rows x [x@w1 | x@w3], the layout the epilogue above reads.
+// A stage is 32 KB per CTA instead of 48, so six stages fit where four did: the loads keep
+// 1.7x as much time in flight, and each CTA reads two thirds of the bytes per FLOP.
+//   Loads of both CTAs complete on the leader's full barrier (cta_group::2 form, no
+//   multicast); the leader's UMMA commits arrive on the matching barrier in both CTAs
+//   (tcgen05.commit with a CTA mask); both CTAs' epilogue warps release an accumulator on
+//   the leader's tempty barrier. TMEM is allocated and freed by one warp in each CTA with
+//   cta_group::2, between cluster barriers.
+// =======================================================================================
+constexpr int kPairStages = 6;
+constexpr int kPairStageBytes = A_BYTES + 2 * B_CHUNK_BYTES;  // 32 KB: x rows + one weight tile
+constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + 1024 + 1024;
+
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void *map, uint32_t bar_cluster,
+                                                 int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const void *map, uint32_t bar_cluster,
+                                                 int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void umma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrives on the barrier at shared::cta address `bar` in both CTAs of the pair once the UMMAs
+// issued so far have completed.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(bar), "h"(static_cast<uint16_t>(0x3))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+template <typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    swiglu_pair_kernel(const __grid_constant__ CUtensorMap tm_x,
+                       const __grid_constant__ CUtensorMap tm_w1,
+                       const __grid_constant__ CUtensorMap tm_w3, T *__restrict__ out,
+                       const Geom g) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kPairStages * kPairStageBytes);
+  uint64_t *full = bars;
+  uint64_t *empty = bars + kPairStages;
+  uint64_t *tfull = bars + 2 * kPairStages;
+  uint64_t *tempty = bars + 2 * kPairStages + 2;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * kPairStages + 4);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int n_pairs = static_cast<int>(gridDim.x >> 1);
+  constexpr bool kBF16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
+  constexpr int kEpiWarps = kEpiThreads / 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), 2 * kEpiWarps);  // both CTAs' epilogue warps
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(rank == 0 ? &tm_w1 : &tm_w3);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_holder), TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const int num_tiles = g.tiles_m * g.tiles_n;  // tiles_m counts 256-row pair tiles
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer (both CTAs) -------------------
+    if (lane == 0) {
+      const void *tm_w = rank == 0 ? &tm_w1 : &tm_w3;
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += n_pairs) {
+        const int m0 = (tile % g.tiles_m) * (2 * BM) + static_cast<int>(rank) * BM;
+        const int n0 = (tile / g.tiles_m) * BN;
+        for (int kb = 0; kb < g.k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1, abort_flag, &g_swiglu_status,
+                         TLLM_DEV_WAIT_TIMEOUT + SITE_EMPTY)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&full[stage]);
+          // The leader's full barrier counts both CTAs' bytes.
+          if (rank == 0) mbar_arrive_expect_tx(fb, 2 * kPairStageBytes);
+          const uint32_t fb_leader = mapa_shared(fb, 0);
+          const uint32_t sa = smem_u32(smem + stage * kPairStageBytes);
+          const int k0 = kb * BK;
+          tma_load_2d_pair(sa, &tm_x, fb_leader, k0, m0);
+          tma_load_3d_pair(sa + A_BYTES, tm_w, fb_leader, 0, k0, n0 >> 6);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // The leader's last commits arrive on this CTA's empty barriers: wait for them before
+      // the CTA may exit.
+      for (int i = 0; ok && i < kPairStages; ++i) {
+        ok = mbar_wait(smem_u32(&empty[stage]), phase ^ 1, abort_flag, &g_swiglu_status,
+                       TLLM_DEV_WAIT_TIMEOUT + SITE_EMPTY);
+        if (++stage == kPairStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ UMMA issuer (leader) -----------------------
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = make_idesc_f16(2 * BM, 2 * BN, kBF16, false, true);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += n_pairs) {
+        if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1, abort_flag, &g_swiglu_status,
+                       TLLM_DEV_WAIT_TIMEOUT + SITE_TEMPTY)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
+        for (int kb = 0; kb < g.k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, &g_swiglu_status,
+                         TLLM_DEV_WAIT_TIMEOUT + SITE_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * kPairStageBytes);
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // A: this CTA's (and the peer's) x rows, K-major, 128B swizzle; B: each CTA's
+            // weight tile, N-major, two 64-column chunks B_CHUNK_BYTES apart.
+            const uint64_t adesc = make_sdesc(sa + k * 32, 16, 1024, kSwizzle128B);
+            const uint64_t bdesc = make_sdesc(sb + k * 2048, B_CHUNK_BYTES, 1024, kSwizzle128B);
+            umma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(smem_u32(&empty[stage]));
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(smem_u32(&tfull[acc]));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // ------------------------------ epilogue (both CTAs) -----------------------
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const uint32_t tempty_leader[2] = {mapa_shared(smem_u32(&tempty[0]), 0),
+                                       mapa_shared(smem_u32(&tempty[1]), 0)};
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = pair; tile < num_tiles; tile += n_pairs) {
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag,
+                                             &g_swiglu_status, TLLM_DEV_WAIT_TIMEOUT + SITE_TFULL)))
+        break;
+      tc_fence_after();
+      const int m0 = (tile % g.tiles_m) * (2 * BM) + static_cast<int>(rank) * BM;
+      const int n0 = (tile / g.tiles_m) * BN;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * ACC_COLS;
+      const int m = m0 + row;
+      T *orow = out + static_cast<int64_t>(m) * g.ldo;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t gr[32], ur[32];
+        tmem_ld32(t_row + c, gr);
+        tmem_ld32(t_row + BN + c, ur);
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float gv = __uint_as_float(gr[j]);
+          const float uv = __uint_as_float(ur[j]);
+          v[j] = (gv / (1.0f + expf(-gv))) * uv;
+        }
+        if (m < g.M) store_row_chunk<T>(orow, n0 + c, g.N, g.vec_store != 0, v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no UMMA, commit or remote arrive of either CTA is still pending
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 // Layout-agnostic fallback (CUDA cores, fp32 accumulation) for shapes whose strides or
 // alignment a TMA descriptor cannot describe: K or N not a multiple of 8, odd strides.
 template <typename T>
@@ -374,10 +630,16 @@ __global__ void __launch_bounds__(256) swiglu_simt_kernel(const T *__restrict__ 
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Kernel choice (tllm_swiglu_variant): the CTA-pair kernel whenever it applies, or forced.
+constexpr int kVariantAuto = 0;
+constexpr int kVariantSingleCta = 1;
+constexpr int kVariantCtaPair = 2;
+
 template <typename T>
 int launch(const void *x, const void *w1, const void *w3, void *out, int64_t M, int64_t N,
            int64_t K, int64_t lda, int64_t ldb1, int64_t ldb3, int64_t ldo, cudaStream_t st,
-           void *const *dsts = nullptr, int ndst = 0, int64_t col_off = 0) {
+           void *const *dsts = nullptr, int ndst = 0, int64_t col_off = 0,
+           int variant = kVariantAuto) {
   const bool tma_ok = lda % 8 == 0 && ldb1 % 8 == 0 && ldb3 % 8 == 0 && aligned16(x) &&
                       aligned16(w1) && aligned16(w3) && K % 8 == 0 && N % 8 == 0;
   if (!tma_ok && ndst > 0)
@@ -445,8 +707,35 @@ int launch(const void *x, const void *w1, const void *w3, void *out, int64_t M, 
   }
   g.vec_store = (ldo % 8 == 0 && col_off % 8 == 0 && dst_aligned &&
                  (ndst > 0 || aligned16(out))) ? 1 : 0;
-  const int num_tiles = g.tiles_m * g.tiles_n;
   const int sms = sm_count();
+  // The CTA pair needs the one-box weight tiles and pays off from two 128-row blocks up.
+  const bool pair_ok = ndst == 0 && w3d && sms >= 2;
+  if (variant == kVariantCtaPair && !pair_ok)
+    return fail(TLLM_ERR_INVALID, "swiglu: the CTA-pair kernel needs N %% 128 == 0 and a local output");
+  if (pair_ok && (variant == kVariantCtaPair || (variant == kVariantAuto && M >= 2 * BM))) {
+    Geom gp = g;
+    gp.tiles_m = static_cast<int>((M + 2 * BM - 1) / (2 * BM));
+    const int pair_tiles = gp.tiles_m * gp.tiles_n;
+    auto kern = swiglu_pair_kernel<T>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(swiglu pair)");
+    // Persistent grid: as many pairs as can be resident at once (clusters are placed on SM
+    // pairs of one GPC).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(sms / 2 * 2));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kPairSmemBytes;
+    cfg.stream = st;
+    int max_clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg);
+    if (e != cudaSuccess) return cuda_status(e, "cudaOccupancyMaxActiveClusters(swiglu pair)");
+    if (max_clusters < 1) return fail(TLLM_ERR_CUDA, "swiglu: the CTA-pair kernel cannot be resident");
+    const int max_pairs = max_clusters < sms / 2 ? max_clusters : sms / 2;
+    const int pairs = pair_tiles < max_pairs ? pair_tiles : max_pairs;
+    kern<<<2 * pairs, kThreads, kPairSmemBytes, st>>>(mx, m1, m3, static_cast<T *>(out), gp);
+    return cuda_status(cudaGetLastError(), "swiglu pair launch");
+  }
+  const int num_tiles = g.tiles_m * g.tiles_n;
   const int grid = num_tiles < sms ? num_tiles : sms;
   if (ndst == 0) {
     auto kern = swiglu_tc_kernel<T, false>;
@@ -491,6 +780,28 @@ extern "C" int tllm_swiglu(const void *x, const void *w1, const void *w3, void *
   if (dtype == TLLM_DTYPE_F16)
     return swiglu::launch<__half>(x, w1, w3, out, M, N, K, lda, ldb1, ldb3, ldo, st);
   return swiglu::launch<__nv_bfloat16>(x, w1, w3, out, M, N, K, lda, ldb1, ldb3, ldo, st);
+}
+
+// tllm_swiglu with an explicit kernel choice, for cross-checking: 0 = automatic, 1 = one CTA
+// per 128 x 128 tile, 2 = the CTA-pair kernel (N a multiple of 128).
+extern "C" int tllm_swiglu_variant(const void *x, const void *w1, const void *w3, void *out,
+                                   int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb1,
+                                   int64_t ldb3, int64_t ldo, int dtype, int variant, void *stream) {
+  using namespace tllm;
+  clear_error();
+  TLLM_CHECK_ARG(variant >= 0 && variant <= 2, "swiglu: unknown kernel variant %d", variant);
+  TLLM_CHECK_ARG(M > 0 && N > 0 && K > 0 && M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31),
+                 "swiglu: dimensions must be positive");
+  TLLM_CHECK_ARG(dtype == TLLM_DTYPE_F16 || dtype == TLLM_DTYPE_BF16, "swiglu: unsupported dtype %d",
+                 dtype);
+  TLLM_CHECK_ARG(x && w1 && w3 && out, "swiglu: null tensor pointer");
+  TLLM_CHECK_ARG(lda >= K && ldb1 >= N && ldb3 >= N && ldo >= N, "swiglu: leading dimension too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == TLLM_DTYPE_F16)
+    return swiglu::launch<__half>(x, w1, w3, out, M, N, K, lda, ldb1, ldb3, ldo, st, nullptr, 0, 0,
+                                  variant);
+  return swiglu::launch<__nv_bfloat16>(x, w1, w3, out, M, N, K, lda, ldb1, ldb3, ldo, st, nullptr, 0,
+                                       0, variant);
 }
 
 extern "C" int tllm_swiglu_colshard(const void *x, const void *w1, const void *w3,
