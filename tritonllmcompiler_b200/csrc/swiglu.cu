@@ -349,8 +349,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 // each CTA's TMEM receives its 128 rows x [x@w1 | x@w3], the layout the epilogue above reads.
 // A stage is 32 KB per CTA instead of 48, so six stages fit where four did: the loads keep
 // 1.7x as much time in flight, and each CTA reads two thirds of the bytes per FLOP.
-//   Loads of both CTAs complete on the leader's full barrier (cta_group::2 form, no
-//   multicast); the leader's UMMA commits arrive on the matching barrier in both CTAs
+//   Each CTA's loads land in its own shared memory and complete on the leader's full barrier
+//   (the cta_group::2 form of the TMA load); the leader's UMMA commits arrive on the matching
+//   barrier in both CTAs
 //   (tcgen05.commit with a CTA mask); both CTAs' epilogue warps release an accumulator on
 //   the leader's tempty barrier. TMEM is allocated and freed by one warp in each CTA with
 //   cta_group::2, between cluster barriers.
