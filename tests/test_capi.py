@@ -73,6 +73,23 @@ def test_invalid_arguments_return_status_and_message():
         _lib.check(rc)
 
 
+def test_extension_entries_validate_arguments():
+    lib = _lib.load()
+    rc = lib.tllm_swiglu_variant(16, 16, 16, 16, 256, 128, 64, 64, 128, 128, 128, 0, 7, None)
+    assert rc == 1 and b"unknown kernel variant 7" in lib.tllm_last_error()
+    rc = lib.tllm_flash_attn_fp8_fwd(16, 16, 16, 16, 1, 1, 64, 64, 96, _arr(96, 96, 96, 1),
+                                     _arr(96, 96, 96, 1), _arr(96, 96, 96, 1), _arr(96, 96, 96, 1),
+                                     0.1, 1.0, 1.0, 1.0, 0, 0, None)
+    assert rc == 1 and b"head dim 96" in lib.tllm_last_error()
+    rc = lib.tllm_flash_attn_fp8_fwd(16, 16, 16, 16, 1, 1, 64, 64, 128, _arr(8192, 8192, 128, 1),
+                                     _arr(8192, 8192, 128, 1), _arr(8192, 8192, 64, 1),
+                                     _arr(8192, 8192, 128, 1), 0.1, 1.0, -1.0, 1.0, 0, 0, None)
+    assert rc == 1 and b"scales" in lib.tllm_last_error()
+    rc = lib.tllm_copy2d_async(16, 64, 16, 32, 64, 4, None)
+    assert rc == 1 and b"pitch" in lib.tllm_last_error()
+    assert lib.tllm_copy2d_async(None, 0, None, 0, 0, 0, None) == 0  # nothing to copy
+
+
 def test_errors_are_thread_local():
     import threading
 
