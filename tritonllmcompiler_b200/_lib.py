@@ -5,6 +5,7 @@ fallback: when the library is missing or fails to load, every operator raises.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 import threading
@@ -167,8 +168,23 @@ def ptr(t: torch.Tensor) -> int:
     return t.data_ptr()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_of(t: torch.Tensor) -> int:
+    """The current CUDA stream of ``t``'s device, as a raw handle."""
+    if _raw_stream is not None:
+        return _raw_stream(t.device.index)
     return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def on_device(t: torch.Tensor):
+    """Context making ``t``'s device current for the library call (the C entry points work on
+    the current device); a no-op when it already is, which is the common case and saves the
+    cost of switching devices on every call."""
+    if t.device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(t.device)
 
 
 def debug_status() -> int:

@@ -4,6 +4,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "common.h"
 
@@ -58,9 +59,110 @@ int sm_count() {
   return g_sm_count[dev];
 }
 
+namespace {
+struct PreparedKernel {
+  const void *kern;
+  int dev, smem, threads, cluster_x;
+  KernelLaunchInfo info;
+};
+std::mutex g_prepared_mutex;
+std::vector<PreparedKernel> g_prepared;
+
+// Everything a tensor map encodes; equal keys give identical maps (a map is a pure function of
+// these), so a cached map is reused whatever memory the address belongs to now.
+struct TmapKey {
+  uint64_t base;
+  uint64_t dims[5];
+  uint64_t strides[4];
+  uint32_t box[5];
+  uint32_t dtype, rank, swizzle, pad;
+};
+struct TmapEntry {
+  bool valid;
+  TmapKey key;
+  CUtensorMap map;
+};
+constexpr int kTmapCacheEntries = 32;
+}  // namespace
+
+int encode_tiled_uncached(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t rank, void *base,
+                          const uint64_t *dims, const uint64_t *strides_bytes, const uint32_t *box,
+                          CUtensorMapSwizzle swizzle);
+
+int prepare_kernel(const void *kern, int smem_bytes, int threads, int cluster_x,
+                   KernelLaunchInfo *out) {
+  const int dev = current_device();
+  if (dev < 0) return TLLM_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_prepared_mutex);
+  for (const PreparedKernel &p : g_prepared) {
+    if (p.kern == kern && p.dev == dev && p.smem == smem_bytes && p.threads == threads &&
+        p.cluster_x == cluster_x) {
+      *out = p.info;
+      return TLLM_OK;
+    }
+  }
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(dynamic shared memory)");
+  cudaFuncAttributes fa;
+  e = cudaFuncGetAttributes(&fa, kern);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncGetAttributes");
+  KernelLaunchInfo info{fa.numRegs, 0};
+  if (cluster_x > 1) {
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_status(e, "cudaDeviceGetAttribute(SM count)");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(sms / cluster_x * cluster_x));
+    cfg.blockDim = dim3(static_cast<unsigned>(threads));
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem_bytes);
+    e = cudaOccupancyMaxActiveClusters(&info.resident, kern, &cfg);
+    if (e != cudaSuccess) return cuda_status(e, "cudaOccupancyMaxActiveClusters");
+  } else {
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&info.resident, kern, threads, smem_bytes);
+    if (e != cudaSuccess) return cuda_status(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  }
+  g_prepared.push_back(PreparedKernel{kern, dev, smem_bytes, threads, cluster_x, info});
+  *out = info;
+  return TLLM_OK;
+}
+
 int encode_tiled(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t rank, void *base,
                  const uint64_t *dims, const uint64_t *strides_bytes, const uint32_t *box,
                  CUtensorMapSwizzle swizzle) {
+  // Per-thread cache of recent maps: repeated calls on the same buffers (a decode loop, a
+  // benchmark) skip the driver call.
+  thread_local TmapEntry cache[kTmapCacheEntries] = {};
+  thread_local int next_slot = 0;
+  TmapKey key;
+  memset(&key, 0, sizeof(key));
+  key.base = reinterpret_cast<uint64_t>(base);
+  for (uint32_t i = 0; i < rank && i < 5; ++i) {
+    key.dims[i] = dims[i];
+    key.box[i] = box[i];
+    if (i + 1 < rank) key.strides[i] = strides_bytes[i];
+  }
+  key.dtype = static_cast<uint32_t>(dtype);
+  key.rank = rank;
+  key.swizzle = static_cast<uint32_t>(swizzle);
+  for (int i = 0; i < kTmapCacheEntries; ++i) {
+    if (cache[i].valid && memcmp(&cache[i].key, &key, sizeof(key)) == 0) {
+      *map = cache[i].map;
+      return TLLM_OK;
+    }
+  }
+  const int rc = encode_tiled_uncached(map, dtype, rank, base, dims, strides_bytes, box, swizzle);
+  if (rc) return rc;
+  TmapEntry &slot = cache[next_slot];
+  next_slot = (next_slot + 1) % kTmapCacheEntries;
+  slot.valid = true;
+  slot.key = key;
+  slot.map = *map;
+  return TLLM_OK;
+}
+
+int encode_tiled_uncached(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t rank, void *base,
+                          const uint64_t *dims, const uint64_t *strides_bytes, const uint32_t *box,
+                          CUtensorMapSwizzle swizzle) {
   std::call_once(g_encode_once, [] {
     void *fn = nullptr;
     cudaDriverEntryPointQueryResult q;

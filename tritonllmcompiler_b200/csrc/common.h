@@ -31,6 +31,18 @@ int encode_tiled(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t rank, voi
                  const uint64_t *dims, const uint64_t *strides_bytes, const uint32_t *box,
                  CUtensorMapSwizzle swizzle);
 
+// Launch attributes of one kernel on the current device: its register count and how many of
+// its CTAs (cluster_x == 1) or clusters (cluster_x > 1) can be resident at once.
+struct KernelLaunchInfo {
+  int num_regs;
+  int resident;
+};
+// Once per (kernel, device, dynamic shared memory, threads, cluster width): raises the kernel's
+// dynamic shared memory limit to smem_bytes and reads its launch attributes; later calls return
+// the cached values without driver calls (the per-call host cost of small launches).
+int prepare_kernel(const void *kern, int smem_bytes, int threads, int cluster_x,
+                   KernelLaunchInfo *out);
+
 // Device error word (one per device image): kernels that give up on a bounded wait
 // record a TLLM_DEV_* code here instead of hanging.
 int read_and_clear_device_status(int *out);

@@ -1272,19 +1272,14 @@ void set_groups(Args &a, int64_t B, int64_t H, int64_t Sk, int64_t row_bytes, in
 template <class GP, typename K>
 int launch_pp(K kern, unsigned grid, const CUtensorMap &mq, const CUtensorMap &mk,
               const CUtensorMap &mv, const Args &a, cudaStream_t st) {
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GP::SMEM_BYTES);
-  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(flash pp)");
+  KernelLaunchInfo info;
+  const int rc = prepare_kernel(reinterpret_cast<const void *>(kern), GP::SMEM_BYTES, kPPThreads, 1, &info);
+  if (rc) return rc;
   // setmaxnreg.inc only completes if the launch holds the registers the split assumes.
-  cudaFuncAttributes fattr;
-  e = cudaFuncGetAttributes(&fattr, kern);
-  if (e != cudaSuccess) return cuda_status(e, "cudaFuncGetAttributes(flash pp)");
-  if (fattr.numRegs != kPPRegsLaunch)
+  if (info.num_regs != kPPRegsLaunch)
     return fail(TLLM_ERR_CUDA, "flash_attention: kernel built with %d registers, %d expected",
-                fattr.numRegs, kPPRegsLaunch);
-  int resident = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kern, kPPThreads, GP::SMEM_BYTES);
-  if (e != cudaSuccess) return cuda_status(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor(flash pp)");
-  if (resident < 1)
+                info.num_regs, kPPRegsLaunch);
+  if (info.resident < 1)
     return fail(TLLM_ERR_CUDA, "flash_attention: the two-tile kernel cannot be resident on this device");
   kern<<<grid, kPPThreads, GP::SMEM_BYTES, st>>>(mq, mk, mv, a);
   return cuda_status(cudaGetLastError(), "flash pp launch");
@@ -1348,8 +1343,9 @@ int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, in
   set_groups(a, B, H, Sk, D * 2, causal);
   if (variant == kVariantSingleTile && !vl) {
     auto kern = flash_fwd_kernel<T, D>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
-    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(flash)");
+    KernelLaunchInfo info;
+    const int rc = prepare_kernel(reinterpret_cast<const void *>(kern), G::SMEM_BYTES, kThreads, 1, &info);
+    if (rc) return rc;
     const unsigned grid = static_cast<unsigned>(B * H * a.n_qtiles);
     kern<<<grid, kThreads, G::SMEM_BYTES, st>>>(mq, mk, mv, a);
     return cuda_status(cudaGetLastError(), "flash launch");

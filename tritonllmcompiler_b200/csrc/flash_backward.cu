@@ -589,7 +589,9 @@ int launch(const void *q, const void *k, const void *v, const void *o, const voi
   a.causal = causal ? 1 : 0;
   if (a.n_ktiles > 0) {
     auto kern = flash_bwd_kernel<T, D>;
-    TLLM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Gm::SMEM_BYTES));
+    KernelLaunchInfo info;
+    const int rc = prepare_kernel(reinterpret_cast<const void *>(kern), Gm::SMEM_BYTES, kThreads, 1, &info);
+    if (rc) return rc;
     const unsigned grid = static_cast<unsigned>(B * H * a.n_ktiles);
     kern<<<grid, kThreads, Gm::SMEM_BYTES, st>>>(mq, mk, mv, mdo, mdq, a);
     TLLM_CUDA_TRY(cudaGetLastError());

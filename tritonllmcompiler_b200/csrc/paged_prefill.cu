@@ -622,8 +622,10 @@ int launch_d(const void *q, const void *kc, const void *vc, void *o, void *ws, c
     a.ws_acc = reinterpret_cast<float *>(static_cast<char *>(ws) + pl.ml_bytes);
   }
   auto kern = paged_prefill_kernel<T, D>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
-  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(paged prefill)");
+  KernelLaunchInfo info;
+  const int rc = prepare_kernel(reinterpret_cast<const void *>(kern), G::SMEM_BYTES, kThreads, 1, &info);
+  if (rc) return rc;
+  cudaError_t e;
   const unsigned grid = static_cast<unsigned>(pl.items * pl.splits);
   kern<<<grid, kThreads, G::SMEM_BYTES, st>>>(mq, mk, mv, a);
   e = cudaGetLastError();

@@ -333,8 +333,9 @@ int launch(const void *x, const void *w, void *out, const Geom &g0, int64_t lda,
   const int sms = sm_count();
   const int grid = num_tiles < sms ? num_tiles : sms;
   auto kern = qkv_norm_rope_kernel<T>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(qkv)");
+  KernelLaunchInfo info;
+  const int rc = prepare_kernel(reinterpret_cast<const void *>(kern), SMEM_BYTES, kThreads, 1, &info);
+  if (rc) return rc;
   kern<<<grid, kThreads, SMEM_BYTES, st>>>(mx, mw, static_cast<T *>(out), g);
   return cuda_status(cudaGetLastError(), "qkv norm rope launch");
 }

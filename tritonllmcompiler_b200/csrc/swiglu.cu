@@ -718,18 +718,12 @@ int launch(const void *x, const void *w1, const void *w3, void *out, int64_t M, 
     gp.tiles_m = static_cast<int>((M + 2 * BM - 1) / (2 * BM));
     const int pair_tiles = gp.tiles_m * gp.tiles_n;
     auto kern = swiglu_pair_kernel<T>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes);
-    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(swiglu pair)");
     // Persistent grid: as many pairs as can be resident at once (clusters are placed on SM
     // pairs of one GPC).
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(sms / 2 * 2));
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kPairSmemBytes;
-    cfg.stream = st;
-    int max_clusters = 0;
-    e = cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg);
-    if (e != cudaSuccess) return cuda_status(e, "cudaOccupancyMaxActiveClusters(swiglu pair)");
+    KernelLaunchInfo info;
+    const int rc = prepare_kernel(reinterpret_cast<const void *>(kern), kPairSmemBytes, kThreads, 2, &info);
+    if (rc) return rc;
+    const int max_clusters = info.resident;
     if (max_clusters < 1) return fail(TLLM_ERR_CUDA, "swiglu: the CTA-pair kernel cannot be resident");
     const int max_pairs = max_clusters < sms / 2 ? max_clusters : sms / 2;
     const int pairs = pair_tiles < max_pairs ? pair_tiles : max_pairs;
@@ -740,15 +734,16 @@ int launch(const void *x, const void *w1, const void *w3, void *out, int64_t M, 
   const int grid = num_tiles < sms ? num_tiles : sms;
   if (ndst == 0) {
     auto kern = swiglu_tc_kernel<T, false>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(swiglu)");
+    KernelLaunchInfo info;
+    const int rc = prepare_kernel(reinterpret_cast<const void *>(kern), SMEM_BYTES, kThreads, 1, &info);
+    if (rc) return rc;
     kern<<<grid, kThreads, SMEM_BYTES, st>>>(mx, m1, m3, static_cast<T *>(out), g);
     return cuda_status(cudaGetLastError(), "swiglu launch");
   }
   auto kern = swiglu_tc_kernel<T, true>;
-  cudaError_t e =
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES_PEERS);
-  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(swiglu peers)");
+  KernelLaunchInfo info;
+  const int rc = prepare_kernel(reinterpret_cast<const void *>(kern), SMEM_BYTES_PEERS, kThreads, 1, &info);
+  if (rc) return rc;
   kern<<<grid, kThreads, SMEM_BYTES_PEERS, st>>>(mx, m1, m3, static_cast<T *>(out), g);
   return cuda_status(cudaGetLastError(), "swiglu peers launch");
 }

@@ -298,8 +298,9 @@ int launch(const void *x, const void *w1t, const void *w3t, void *out, int64_t M
   const int sms = sm_count();
   const int grid = num_tiles < sms ? num_tiles : sms;
   auto kern = swiglu_fp8_kernel<T>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(swiglu fp8)");
+  KernelLaunchInfo info;
+  const int rc = prepare_kernel(reinterpret_cast<const void *>(kern), SMEM_BYTES, kThreads, 1, &info);
+  if (rc) return rc;
   kern<<<grid, kThreads, SMEM_BYTES, st>>>(mx, m1, m3, static_cast<T *>(out), g);
   return cuda_status(cudaGetLastError(), "swiglu fp8 launch");
 }

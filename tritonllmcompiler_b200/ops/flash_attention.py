@@ -39,7 +39,7 @@ def flash_attention(q, k, v, *, causal: bool = False, sm_scale: float | None = N
     v2 = v if _tma_ready(v) else v.contiguous()
     out = torch.empty((b, h, seqlen_q, d), device=q.device, dtype=q.dtype)
     lib = _lib.load()
-    with torch.cuda.device(q.device):
+    with _lib.on_device(q):
         _lib.check(
             lib.tllm_flash_attn_fwd(
                 q2.data_ptr(), k2.data_ptr(), v2.data_ptr(), out.data_ptr(),

@@ -33,7 +33,7 @@ def flash_attention_fwd_lse(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *
     lse = torch.empty((b, h, sq), device=q.device, dtype=torch.float32)
     if b * h * sq == 0:
         return o, lse
-    with torch.cuda.device(q.device):
+    with _lib.on_device(q):
         _lib.check(_lib.load().tllm_flash_attn_fwd_lse(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), b, h, sq, sk, d,
             _lib.strides(q), _lib.strides(k), _lib.strides(v), _lib.strides(o), float(sm_scale),
@@ -63,7 +63,7 @@ def flash_attention_backward(q, k, v, o, lse, dout, *, causal: bool = False,
     if b * h == 0 or (sq == 0 and sk == 0):
         return dq, dk, dv
     lib = _lib.load()
-    with torch.cuda.device(q.device):
+    with _lib.on_device(q):
         ws_bytes = lib.tllm_flash_attn_bwd_workspace_size(b, h, sq, d)
         ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=q.device)
         _lib.check(lib.tllm_flash_attn_bwd(

@@ -68,7 +68,7 @@ def flash_attention_fp8(q8: torch.Tensor, k8: torch.Tensor, vt8: torch.Tensor, s
     k8 = k8 if _strides_ok(k8) else k8.contiguous()
     if not _strides_ok(vt8):
         vt8 = transpose_v_e4m3(vt8.transpose(-1, -2))
-    with torch.cuda.device(q8.device):
+    with _lib.on_device(q8):
         _lib.check(_lib.load().tllm_flash_attn_fp8_fwd(
             q8.data_ptr(), k8.data_ptr(), vt8.data_ptr(), out.data_ptr(), b, h, sq, sk, d,
             _lib.strides(q8), _lib.strides(k8), _lib.strides(vt8), _lib.strides(out),

@@ -48,7 +48,7 @@ def flash_attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     cq = cu_seqlens_q.to(torch.int32).contiguous()
     ck = cu_seqlens_k.to(torch.int32).contiguous()
     lib = _lib.load()
-    with torch.cuda.device(q.device):
+    with _lib.on_device(q):
         _lib.check(lib.tllm_flash_attn_varlen_fwd(
             qq.data_ptr(), kk.data_ptr(), vv.data_ptr(), out.data_ptr(), cq.data_ptr(),
             ck.data_ptr(), b, h, hkv, total_q, total_k, int(max_seqlen_q), int(max_seqlen_k), d,

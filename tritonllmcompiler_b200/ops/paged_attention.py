@@ -51,7 +51,7 @@ def paged_attention(
     kc = k_cache if cache_ok(k_cache) else k_cache.contiguous()
     vc = v_cache if cache_ok(v_cache) else v_cache.contiguous()
     lib = _lib.load()
-    with torch.cuda.device(q.device):
+    with _lib.on_device(q):
         ws_bytes = lib.tllm_paged_attn_workspace_size(b, h, d, block_size, max_blocks)
         ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
         _lib.check(

@@ -54,7 +54,7 @@ def paged_kv_append(k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Ten
     if b * t * h == 0:
         return
     lib = _lib.load()
-    with torch.cuda.device(k_new.device):
+    with _lib.on_device(k_new):
         _lib.check(lib.tllm_paged_kv_append(
             kn.data_ptr(), vn.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), bt.data_ptr(),
             sp.data_ptr(), None if nn is None else nn.data_ptr(), b, t, h, d, block_size,
@@ -81,7 +81,7 @@ def paged_kv_append_rope(k_new: torch.Tensor, v_new: torch.Tensor, weight: torch
     cs = cos if _vec_ok(cos) else cos.contiguous()
     sn = sin if _vec_ok(sin) else sin.contiguous()
     lib = _lib.load()
-    with torch.cuda.device(k_new.device):
+    with _lib.on_device(k_new):
         _lib.check(lib.tllm_paged_kv_append_rope(
             kn.data_ptr(), vn.data_ptr(), w.data_ptr(), cs.data_ptr(), sn.data_ptr(),
             cs.shape[0], cs.stride(0), sn.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
@@ -124,7 +124,7 @@ def paged_attention_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
     bt = block_tables if block_tables.dtype == torch.int32 else block_tables.to(torch.int32)
     cl = context_lens.to(torch.int32).contiguous()
     lib = _lib.load()
-    with torch.cuda.device(q.device):
+    with _lib.on_device(q):
         ws_bytes = lib.tllm_paged_prefill_workspace_size(b, hq, hkv, sq, d, block_size,
                                                          bt.shape[1])
         ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)

@@ -34,7 +34,7 @@ def qkv_norm_rope(x: torch.Tensor, w: torch.Tensor, wq: torch.Tensor, wk: torch.
     x, w = (t if t.stride(1) == 1 and t.stride(0) % 8 == 0 else t.contiguous() for t in (x, w))
     cos, sin = cos.contiguous(), sin.contiguous()
     pos = positions.to(torch.int32).contiguous()
-    with torch.cuda.device(x.device):
+    with _lib.on_device(x):
         _lib.check(_lib.load().tllm_qkv_norm_rope(
             x.data_ptr(), w.data_ptr(), wq.contiguous().data_ptr(), wk.contiguous().data_ptr(),
             cos.data_ptr(), sin.data_ptr(), cos.shape[0], cos.stride(0), sin.stride(0),

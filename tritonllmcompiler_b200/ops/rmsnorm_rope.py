@@ -34,7 +34,7 @@ def rmsnorm_rope(
     if out.numel() == 0:
         return out
     lib = _lib.load()
-    with torch.cuda.device(x.device):
+    with _lib.on_device(x):
         _lib.check(
             lib.tllm_rmsnorm_rope(
                 x.data_ptr(), w.data_ptr(), c.data_ptr(), sn.data_ptr(), out.data_ptr(),

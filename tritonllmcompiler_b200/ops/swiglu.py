@@ -25,7 +25,7 @@ def swiglu(x: torch.Tensor, w1: torch.Tensor, w3: torch.Tensor) -> torch.Tensor:
     a1 = w1 if w1.stride(1) == 1 and w1.stride(0) >= max(n, 1) else w1.contiguous()
     a3 = w3 if w3.stride(1) == 1 and w3.stride(0) >= max(n, 1) else w3.contiguous()
     lib = _lib.load()
-    with torch.cuda.device(x.device):
+    with _lib.on_device(x):
         _lib.check(
             lib.tllm_swiglu(
                 x2.data_ptr(), a1.data_ptr(), a3.data_ptr(), out.data_ptr(), m, n, k,

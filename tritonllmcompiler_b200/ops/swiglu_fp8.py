@@ -33,7 +33,7 @@ def swiglu_fp8(x8: torch.Tensor, w1t8: torch.Tensor, w3t8: torch.Tensor, scale_x
     if m == 0 or n == 0:
         return out
     x8, w1t8, w3t8 = (t if t.stride(1) == 1 else t.contiguous() for t in (x8, w1t8, w3t8))
-    with torch.cuda.device(x8.device):
+    with _lib.on_device(x8):
         _lib.check(_lib.load().tllm_swiglu_fp8(
             x8.data_ptr(), w1t8.data_ptr(), w3t8.data_ptr(), out.data_ptr(), m, n, k, x8.stride(0),
             w1t8.stride(0), w3t8.stride(0), out.stride(0), float(scale_x), float(scale_w1),
