@@ -18,7 +18,11 @@ def _tables(p, d, dtype):
 
 
 @pytest.mark.parametrize("m,k,hq,hkv,dtype", [(256, 512, 4, 2, torch.float16), (300, 1024, 8, 1, torch.float16),
-                                              (64, 256, 3, 1, torch.bfloat16), (130, 4096, 2, 2, torch.float16)])
+                                              (64, 256, 3, 1, torch.bfloat16), (130, 4096, 2, 2, torch.float16),
+                                              # more tiles than SMs: the partial last wave runs as
+                                              # one-head tiles (11 heads: one of them is past the end)
+                                              (2048, 512, 16, 4, torch.float16),
+                                              (4096, 256, 7, 2, torch.bfloat16)])
 def test_qkv_norm_rope_matches_oracle(cuda_device, m, k, hq, hkv, dtype):
     g = torch.Generator().manual_seed(m + k)
     n = (hq + 2 * hkv) * 128

@@ -69,7 +69,27 @@ struct Geom {
   const int32_t *positions;  // [M]
   int rope_rows;
   float eps;
+  // Tiles 0 .. n_wide-1 are 128 rows x 2 heads; the wide tiles that would form a partial last
+  // wave are instead split into n_narrow tiles of one head each (half as long), numbered after
+  // them.
+  int n_wide, n_narrow;
 };
+
+// Rows, first head and head count of tile `tile` (0 heads: a one-head tile past the last head,
+// skipped by every role).
+__device__ __forceinline__ void tile_geo(const Geom &g, int tile, int &m0, int &head0, int &nheads) {
+  if (tile < g.n_wide) {
+    m0 = (tile % g.tiles_m) * BM;
+    head0 = (tile / g.tiles_m) * 2;
+    nheads = 2;
+    return;
+  }
+  const int i = tile - g.n_wide;
+  const int t = g.n_wide + (i >> 1);
+  m0 = (t % g.tiles_m) * BM;
+  head0 = (t / g.tiles_m) * 2 + (i & 1);
+  nheads = head0 < g.Hq + 2 * g.Hkv ? 1 : 0;
+}
 
 template <typename T>
 __device__ __forceinline__ float round_io(float v) {
@@ -91,7 +111,7 @@ __device__ __forceinline__ void ld8(const T *p, float (&v)[8]) {
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     qkv_norm_rope_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                         T *__restrict__ out, const Geom g) {
+                         const __grid_constant__ CUtensorMap tm_w1, T *__restrict__ out, const Geom g) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -119,6 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tm_x);
     tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_w1);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
@@ -128,7 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
-  const int num_tiles = g.tiles_m * g.tiles_n;
+  const int num_tiles = g.n_wide + g.n_narrow;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -136,8 +157,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile % g.tiles_m) * BM;
-        const int n0 = (tile / g.tiles_m) * 2 * HD;
+        int m0, head0, nheads;
+        tile_geo(g, tile, m0, head0, nheads);
+        if (nheads == 0) continue;
         for (int kb = 0; kb < g.k_blocks; ++kb) {
           if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1, abort_flag, &g_qkv_status,
                          TLLM_DEV_WAIT_TIMEOUT + SITE_EMPTY)) {
@@ -145,13 +167,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const uint32_t fb = smem_u32(&full[stage]);
-          mbar_arrive_expect_tx(fb, STAGE_BYTES);
+          mbar_arrive_expect_tx(fb, A_BYTES + nheads * 2 * B_CHUNK_BYTES);
           const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
           const uint32_t sb = sa + A_BYTES;
           const int k0 = kb * BK;
           tma_load_2d(sa, &tm_x, fb, k0, m0);
-          // All four 64-column chunks of the [BK x 256] weight tile in one box.
-          tma_load_3d(sb, &tm_w, fb, 0, k0, n0 >> 6);
+          // All 64-column chunks of the [BK x 128 * nheads] weight tile in one box.
+          tma_load_3d(sb, nheads == 2 ? &tm_w : &tm_w1, fb, 0, k0, head0 * 2);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -161,13 +183,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = make_idesc_f16(BM, 2 * HD, kBF16, false, true);
+      const uint32_t idesc2 = make_idesc_f16(BM, 2 * HD, kBF16, false, true);
+      const uint32_t idesc1 = make_idesc_f16(BM, HD, kBF16, false, true);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int m0, head0, nheads;
+        tile_geo(g, tile, m0, head0, nheads);
+        if (nheads == 0) continue;
+        const uint32_t idesc = nheads == 2 ? idesc2 : idesc1;
         if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1, abort_flag, &g_qkv_status,
                        TLLM_DEV_WAIT_TIMEOUT + SITE_TEMPTY)) {
           ok = false;
@@ -211,19 +238,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int m0, h0, nheads;
+      tile_geo(g, tile, m0, h0, nheads);
+      if (nheads == 0) continue;
       if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag, &g_qkv_status,
                      TLLM_DEV_WAIT_TIMEOUT + SITE_TFULL))
         break;
       tc_fence_after();
-      const int m0 = (tile % g.tiles_m) * BM;
-      const int h0 = (tile / g.tiles_m) * 2;
       const int m = m0 + row;
       const bool mv = m < g.M;
       int pos = mv ? __ldg(g.positions + m) : 0;
       pos = min(max(pos, 0), g.rope_rows - 1);
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * ACC_COLS;
 #pragma unroll 1
-      for (int hh = 0; hh < 2; ++hh) {
+      for (int hh = 0; hh < nheads; ++hh) {
         const int head = h0 + hh;
         if (head >= heads) break;
         // The projection, rounded to the I/O dtype (what a separate GEMM would store).
@@ -307,7 +335,7 @@ int launch(const void *x, const void *w, void *out, const Geom &g0, int64_t lda,
            cudaStream_t st) {
   const CUtensorMapDataType dt =
       std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  CUtensorMap mx, mw;
+  CUtensorMap mx, mw, mw1;
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(g0.K), static_cast<uint64_t>(g0.M)};
     const uint64_t str[1] = {static_cast<uint64_t>(lda) * 2};
@@ -324,19 +352,28 @@ int launch(const void *x, const void *w, void *out, const Geom &g0, int64_t lda,
     const uint32_t box[3] = {64, BK, 4};
     int rc = encode_tiled(&mw, dt, 3, const_cast<void *>(w), dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
+    const uint32_t box1[3] = {64, BK, 2};  // one head
+    rc = encode_tiled(&mw1, dt, 3, const_cast<void *>(w), dims, str, box1, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
   }
   Geom g = g0;
   g.tiles_m = (g.M + BM - 1) / BM;
   g.tiles_n = (g.N + 2 * HD - 1) / (2 * HD);
   g.k_blocks = (g.K + BK - 1) / BK;
-  const int num_tiles = g.tiles_m * g.tiles_n;
-  const int sms = sm_count();
-  const int grid = num_tiles < sms ? num_tiles : sms;
+  const int wide_all = g.tiles_m * g.tiles_n;
+  const int sms = sm_count() > 0 ? sm_count() : 148;
+  const int grid = wide_all < sms ? wide_all : sms;
+  // A partial last wave of wide tiles would keep a few SMs busy for a whole tile while the
+  // rest wait: those tiles run as two one-head tiles each, half as long, on twice the SMs.
+  const int rest = wide_all % grid;
+  const bool split = wide_all > grid && rest > 0 && 2 * rest <= grid;
+  g.n_wide = split ? wide_all - rest : wide_all;
+  g.n_narrow = split ? 2 * rest : 0;
   auto kern = qkv_norm_rope_kernel<T>;
   KernelLaunchInfo info;
   const int rc = prepare_kernel(reinterpret_cast<const void *>(kern), SMEM_BYTES, kThreads, 1, &info);
   if (rc) return rc;
-  kern<<<grid, kThreads, SMEM_BYTES, st>>>(mx, mw, static_cast<T *>(out), g);
+  kern<<<grid, kThreads, SMEM_BYTES, st>>>(mx, mw, mw1, static_cast<T *>(out), g);
   return cuda_status(cudaGetLastError(), "qkv norm rope launch");
 }
 
