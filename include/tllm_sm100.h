@@ -327,6 +327,15 @@ TLLM_API int tllm_swiglu_fp8(const void *x, const void *w1t, const void *w3t, vo
                              int64_t ldb3, int64_t ldo, float scale_x, float scale_w1,
                              float scale_w3, int out_dtype, void *stream);
 
+/* Same as tllm_swiglu_fp8 with an explicit kernel choice, for cross-checking: 0 = automatic
+ * (the CTA-pair kernel when M >= 256), 1 = one CTA per 128 x 128 output tile, 2 = the
+ * CTA-pair kernel (two CTAs on two SMs share 256 x 128 output tiles through
+ * tcgen05.mma.cta_group::2). */
+TLLM_API int tllm_swiglu_fp8_variant(const void *x, const void *w1t, const void *w3t, void *out,
+                                     int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb1,
+                                     int64_t ldb3, int64_t ldo, float scale_x, float scale_w1,
+                                     float scale_w3, int out_dtype, int variant, void *stream);
+
 /*
  * FP8 flash attention forward: softmax(sm_scale * (scale_q q)(scale_k k)^T) (scale_v v) with
  * e4m3 inputs and per-tensor scales, on the tcgen05 kind::f8f6f4 path; an extension of

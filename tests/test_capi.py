@@ -77,6 +77,9 @@ def test_extension_entries_validate_arguments():
     lib = _lib.load()
     rc = lib.tllm_swiglu_variant(16, 16, 16, 16, 256, 128, 64, 64, 128, 128, 128, 0, 7, None)
     assert rc == 1 and b"unknown kernel variant 7" in lib.tllm_last_error()
+    rc = lib.tllm_swiglu_fp8_variant(16, 16, 16, 16, 256, 128, 64, 64, 64, 64, 128, 1.0, 1.0, 1.0,
+                                     0, 3, None)
+    assert rc == 1 and b"unknown kernel variant 3" in lib.tllm_last_error()
     rc = lib.tllm_flash_attn_fp8_fwd(16, 16, 16, 16, 1, 1, 64, 64, 96, _arr(96, 96, 96, 1),
                                      _arr(96, 96, 96, 1), _arr(96, 96, 96, 1), _arr(96, 96, 96, 1),
                                      0.1, 1.0, 1.0, 1.0, 0, 0, None)

@@ -44,3 +44,34 @@ def test_fp8_swiglu_strided_output_rows(cuda_device):
     big[:, :256] = x8
     b = swiglu_fp8(big.cuda()[:, :256], w18.cuda(), w38.cuda(), sx, s1, s3)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("m,n,k,out_dtype,variants", [
+    (256, 128, 128, torch.float16, (1, 2)),
+    (300, 200, 1040, torch.float16, (1, 2)),     # ragged M, N and K: zero-filled edge tiles
+    (128, 384, 512, torch.bfloat16, (1, 2)),     # forced pair with the second CTA's rows past M
+    (1000, 640, 528, torch.bfloat16, (1, 2, 0)),
+    (4096, 1024, 4096, torch.float16, (1, 2, 0)),
+])
+def test_fp8_swiglu_kernel_variants_agree(cuda_device, m, n, k, out_dtype, variants):
+    """The CTA-pair kernel (tcgen05.mma.cta_group::2, two SMs per 256 x 128 tile) and the
+    one-CTA kernel accumulate every output element in the same K order: bit-identical; the
+    automatic choice (0) takes the pair kernel from M >= 256."""
+    g = torch.Generator().manual_seed(m * 7 + n + k)
+    x8, sx = quantize_e4m3(torch.randn(m, k, generator=g))
+    w18, s1 = quantize_e4m3(torch.randn(n, k, generator=g) / k ** 0.5)
+    w38, s3 = quantize_e4m3(torch.randn(n, k, generator=g) / k ** 0.5)
+    x8, w18, w38 = x8.cuda(), w18.cuda(), w38.cuda()
+    outs = []
+    for variant in variants:
+        o = torch.full((m, n), float("nan"), dtype=out_dtype, device="cuda")
+        _lib.check(_lib.load().tllm_swiglu_fp8_variant(
+            x8.data_ptr(), w18.data_ptr(), w38.data_ptr(), o.data_ptr(), m, n, k, k, k, k, n,
+            sx, s1, s3, _lib.DTYPE_CODES[out_dtype], variant,
+            torch.cuda.current_stream().cuda_stream))
+        outs.append(o)
+    for o in outs[1:]:
+        assert torch.equal(outs[0], o)
+    assert not torch.isnan(outs[0]).any()
+    assert torch.equal(outs[0], swiglu_fp8(x8, w18, w38, sx, s1, s3, out_dtype))
+    assert _lib.debug_status() == 0

@@ -103,6 +103,11 @@ SIGNATURES = {
         [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float,
          ctypes.c_float, ctypes.c_float, ctypes.c_int, _vp],
     ),
+    "tllm_swiglu_fp8_variant": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float,
+         ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_int, _vp],
+    ),
     "tllm_flash_attn_fp8_fwd": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _c_i64p, _c_i64p, _c_i64p, _c_i64p,
