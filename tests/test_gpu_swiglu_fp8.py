@@ -51,6 +51,8 @@ def test_fp8_swiglu_strided_output_rows(cuda_device):
     (300, 200, 1040, torch.float16, (1, 2)),     # ragged M, N and K: zero-filled edge tiles
     (128, 384, 512, torch.bfloat16, (1, 2)),     # forced pair with the second CTA's rows past M
     (1000, 640, 528, torch.bfloat16, (1, 2, 0)),
+    (260, 100, 256, torch.float16, (1, 2, 0)),    # ldo = 100: the scalar-store epilogue
+    (256, 48, 16, torch.bfloat16, (1, 2)),        # K = 16: one k block, mostly zero-filled
     (4096, 1024, 4096, torch.float16, (1, 2, 0)),
 ])
 def test_fp8_swiglu_kernel_variants_agree(cuda_device, m, n, k, out_dtype, variants):
