@@ -124,8 +124,11 @@ TLLM_API int tllm_paged_attn_decode(const void *q, const void *k_cache, const vo
  * library of TLLM_PAGED_NOALLOC_SCRATCH_BYTES bytes; a problem whose partials need more
  * (tllm_paged_attn_workspace_size above that limit) is rejected with TLLM_ERR_WORKSPACE and
  * nothing is launched. The caller still provides every input and the output.
- *   - The first call on a device looks up the array's device address (once per device, with
- *     that device current); make that first call before any stream capture.
+ *   - Each call looks up the array's device address with the caller's device current
+ *     (cudaGetSymbolAddress, so the address stays right after a cudaDeviceReset); the first
+ *     call on a device also loads the library's device code there, so make that first call
+ *     before any stream capture.
+ *   - Dimensions are checked (TLLM_ERR_INVALID) before the scratch size is planned.
  *   - All calls share the one array and it keeps the last call's contents. Calls whose
  *     kernels can overlap on the GPU (different streams, no ordering between them) race on
  *     it and may return wrong results; order such calls on one stream or with events.

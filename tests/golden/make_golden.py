@@ -2,7 +2,7 @@
 
 Run in a checkout where xdlhzdh/TritonLLMCompiler is present (read-only is fine):
 
-    python tests/golden/make_golden.py [path/to/TritonLLMCompiler]
+    python tests/golden/make_golden.py path/to/TritonLLMCompiler
 
 It imports ``triton_llm.reference`` from ``<reference>/python`` (CPU only: those functions
 are plain PyTorch), builds the cases of the reference's op tests (tests/python/test_*.py:
@@ -195,4 +195,8 @@ def main(root: str):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    # The reference checkout is given explicitly: the first argument, or TRITON_LLM_REFERENCE.
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("TRITON_LLM_REFERENCE")
+    if not ref_root:
+        sys.exit("usage: make_golden.py <reference checkout> (or set TRITON_LLM_REFERENCE)")
+    main(ref_root)

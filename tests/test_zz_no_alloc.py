@@ -72,6 +72,9 @@ def test_no_alloc_matches_workspace_entry_point_on_two_calls(cuda_device):
         rc, out = _no_alloc(lib, q, kc, vc, bt, cl, bs)
         _lib.check(rc)
         torch.cuda.synchronize()
+        # Both entry points plan the same splits and run the same kernels in the same order,
+        # so anything short of bit equality means stale or misplaced scratch.
+        assert torch.equal(out, ref)
         assert torch.allclose(out.float(), ref.float(), **G.tol(out.dtype))
 
 
@@ -87,3 +90,15 @@ def test_no_alloc_rejects_problems_beyond_its_array(cuda_device):
                                             s4, s4c, s4c, s2, s4, 0.1, 0, None)
     assert rc == 3
     assert b"fixed" in lib.tllm_last_error()
+
+
+def test_no_alloc_rejects_bad_dimensions_before_sizing(cuda_device):
+    """A negative batch or an unsupported head dim is an argument error, not a scratch overflow."""
+    lib = _lib.load()
+    s4 = (ctypes.c_int64 * 4)(1, 1, 1, 1)
+    s4c = (ctypes.c_int64 * 4)(16 * 8 * 128, 8 * 128, 128, 1)
+    s2 = (ctypes.c_int64 * 2)(4, 1)
+    for b, h, d, bs in [(-1, 8, 128, 16), (4, -3, 128, 16), (4, 8, 96, 16), (4, 8, 128, 8)]:
+        rc = lib.tllm_paged_attn_decode_noalloc(16, 16, 16, 16, 16, 16, b, h, d, bs, 4, 8,
+                                                s4, s4c, s4c, s2, s4, 0.1, 0, None)
+        assert rc == 1, (b, h, d, bs)

@@ -16,7 +16,6 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
-#include <mutex>
 
 #include "common.h"
 #include "paged_attention.cuh"
@@ -417,24 +416,16 @@ namespace {
 
 __device__ __align__(256) unsigned char g_noalloc_scratch[TLLM_PAGED_NOALLOC_SCRATCH_BYTES];
 
-std::mutex g_noalloc_mutex;
-void *g_noalloc_ptr[64] = {};
-
 // Device address of g_noalloc_scratch on the current device. In host code the symbol name
-// only stands in for the device array, so the address is looked up once per device (with
-// that device current) and cached.
+// only stands in for the device array, so the address is looked up with the device current.
+// It is looked up on every call rather than cached: a cached address would go stale after
+// cudaDeviceReset() gives the device a new context, and the lookup costs well under a
+// microsecond once the module is loaded (the first call on a device loads it).
 int noalloc_scratch(void **out) {
-  int dev = -1;
-  TLLM_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64) return fail(TLLM_ERR_CUDA, "paged_attention: device %d out of range", dev);
-  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (!g_noalloc_ptr[dev]) {
-    void *p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(paged no-alloc scratch)");
-    g_noalloc_ptr[dev] = p;
-  }
-  *out = g_noalloc_ptr[dev];
+  void *p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(paged no-alloc scratch)");
+  *out = p;
   return TLLM_OK;
 }
 
@@ -457,6 +448,14 @@ extern "C" int tllm_paged_attn_decode_noalloc(const void *q, const void *k_cache
                  "paged_attention_noalloc: unsupported dtype %d", dtype);
   TLLM_CHECK_ARG(sq && skc && svc && sbt && so, "paged_attention_noalloc: null stride array");
   TLLM_CHECK_ARG(max_blocks >= 0 && num_blocks >= 0, "paged_attention_noalloc: negative table size");
+  // Dimensions are checked before the scratch size is planned from them: a negative B or H
+  // would otherwise wrap the size around and be reported as a scratch overflow.
+  TLLM_CHECK_ARG(B >= 0 && H >= 0, "paged_attention_noalloc: negative dimension");
+  TLLM_CHECK_ARG(D == 16 || D == 32 || D == 64 || D == 128,
+                 "paged_attention_noalloc: head dim %lld not in {16,32,64,128}", (long long)D);
+  TLLM_CHECK_ARG(block_size == 16 || block_size == 32 || block_size == 64,
+                 "paged_attention_noalloc: block_size %lld not in {16,32,64}",
+                 (long long)block_size);
   if (B == 0 || H == 0) return TLLM_OK;
   TLLM_CHECK_ARG(q && k_cache && v_cache && block_tables && context_lens && o,
                  "paged_attention_noalloc: null tensor pointer");

@@ -62,6 +62,11 @@ class SwigluHostPipeline:
             self.s_out = torch.cuda.Stream(self.device)
             self.ev_in = [torch.cuda.Event() for _ in self.blocks]
             self.ev_done = [torch.cuda.Event() for _ in self.blocks]
+            # Recorded on s_out at the end of every call: the next call's uploads and kernels
+            # wait for it, so they never overwrite buffers the previous call still reads, even
+            # when the caller switches streams between calls.
+            self.ev_end = torch.cuda.Event()
+            self.ev_end.record(self.s_out)
 
     def __call__(self, x: torch.Tensor, w1: torch.Tensor, w3: torch.Tensor,
                  out: torch.Tensor | None = None) -> torch.Tensor:
@@ -83,6 +88,7 @@ class SwigluHostPipeline:
             cur = torch.cuda.current_stream(self.device)
             for s in (self.s_in, self.s_comp, self.s_out):
                 s.wait_stream(cur)
+                s.wait_event(self.ev_end)
             sin, scomp, sout = (s.cuda_stream for s in (self.s_in, self.s_comp, self.s_out))
             # host -> device: x, then the weight blocks in order
             _lib.check(lib.tllm_copy2d_async(self.dx.data_ptr(), k * es, x.data_ptr(), k * es,
@@ -106,6 +112,7 @@ class SwigluHostPipeline:
                 _lib.check(lib.tllm_copy2d_async(out.data_ptr() + c0 * es, n * es,
                                                  self.dout.data_ptr() + c0 * es, n * es,
                                                  (c1 - c0) * es, m, sout))
+            self.ev_end.record(self.s_out)
             cur.wait_stream(self.s_out)
         return out
 
