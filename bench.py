@@ -5,9 +5,21 @@ Headline workload (N=1): swiglu at the Llama-3-8B MLP shape, x [4096, 4096], w1/
 [4096, 14336] fp16 (seed 1), metric TFLOP/s = 4*M*N*K / time. With N GPUs (torchrun, one
 process per GPU) the same problem is column-sharded over N (each rank computes
 out[:, N/g slice]); the GEMM epilogue stores each tile into every rank's [M, N] output over
-NVLink (CUDA IPC peer buffers), or with --comm nccl the slices are all-gathered (strong scaling).
-At N=1 the line also carries the other three operators at their configurations under
-"ops" (rmsnorm_rope, flash_attention causal/non-causal, paged_attention decode).
+NVLink (CUDA IPC peer buffers) and synchronises with the peers inside the kernel, or with
+--comm nccl the slices are all-gathered (strong scaling). At N>1 every rank checks 256
+sampled rows of its gathered output bit for bit against the single-GPU operator.
+
+Also on the line:
+* "ops" (N=1): the other three operators at their configurations (rmsnorm_rope,
+  flash_attention causal/non-causal, paged_attention decode) and the extensions, each with a
+  roofline; the four reference operators also with a CPU baseline (the oracle on the host
+  cores, sampled and extrapolated where the full problem is too large) and an end-to-end
+  figure through the public operator with pinned host inputs and result copied every step.
+* "sharded_cfg5" (every N): the Llama-3-70B-shaped sharded workloads -- swiglu
+  x [8192, 8192], w [8192, 28672] column-sharded with the output gathered; causal
+  flash_attention [8, 64, 8192, 128] head-sharded; paged decode B256 H64 D128 bs32, lens
+  U[1024, 32768], batch-sharded over a token-balanced partition -- whole-job throughput from
+  the max-over-ranks device time.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -31,8 +43,14 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# Measured peer-copy rate per direction per GPU over NVLink on this pool (nominal 900 GB/s).
+NVLINK_GBS = 770.0
 SWIGLU_SHAPE = (4096, 4096, 14336)  # M, K, N
+CFG5_SWIGLU = (8192, 8192, 28672)  # M, K, N
+CFG5_FLASH = (8, 64, 8192, 128)  # B, H, S, D (causal)
+CFG5_PAGED = (256, 64, 128, 32, 1024, 32768)  # B, H, D, block_size, min len, max len
 L2_FLUSH_BYTES = 256 << 20
+PARITY_ROWS = (1920, 2176)  # sampled row block of the headline output
 
 
 def parse():
@@ -42,7 +60,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-ops", action="store_true", help="skip the per-operator extras")
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
+    ap.add_argument("--no-cfg5", action="store_true", help="skip the 70B-shaped sharded workloads")
     ap.add_argument("--chunks", type=int, default=1,
                     help="N>1 with --comm nccl: row chunks whose all-gather overlaps the next GEMM")
     ap.add_argument("--e2e-chunks", type=int, default=8,
@@ -165,54 +184,164 @@ def _events_time(torch, fn, steps, warmup, flush=None):
     return [a.elapsed_time(b) for a, b in times]
 
 
-def _cpu_threads():
+# ------------------------------------------------------------------------------------------
+# CPU baselines: the oracle (a numpy restatement of the reference's own *_ref functions) on
+# the host cores, on seeded inputs of the workload's shapes and distributions.
+def cpu_cores() -> int:
     try:
-        from threadpoolctl import threadpool_info
-
-        n = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
-        if n:
-            return max(n)
+        return len(os.sched_getaffinity(0))
     except Exception:
-        pass
-    return os.cpu_count() or 1
+        return os.cpu_count() or 1
 
 
-def cpu_swiglu_inputs(rows=512):
-    """A row sample of the swiglu workload for the CPU oracle (fp16-representable fp32)."""
+def _blas_threads(n: int):
+    """Context setting the BLAS pool to n threads (torchrun starts ranks with one)."""
+    try:
+        from threadpoolctl import threadpool_limits
+
+        return threadpool_limits(limits=n, user_api="blas")
+    except Exception:
+        import contextlib
+
+        return contextlib.nullcontext()
+
+
+def _normal_f16(rng, shape, scale=1.0, reservoir=1 << 22):
+    """fp16-representable float32 array of N(0, scale^2) values. Large arrays repeat a seeded
+    reservoir (values only feed timing samples there)."""
     import numpy as np
 
     from oracle import ops_oracle as O
 
-    M, K, N = SWIGLU_SHAPE
-    rng = np.random.default_rng(1)
-    x = O.round_to(rng.standard_normal((rows, K), dtype=np.float32), "fp16")
-    w1 = O.round_to(rng.standard_normal((K, N), dtype=np.float32) / np.float32(math.sqrt(K)), "fp16")
-    w3 = O.round_to(rng.standard_normal((K, N), dtype=np.float32) / np.float32(math.sqrt(K)), "fp16")
+    n = int(np.prod(shape))
+    if n <= reservoir:
+        return O.round_to(rng.standard_normal(shape, dtype=np.float32) * np.float32(scale), "fp16")
+    base = O.round_to(rng.standard_normal(reservoir, dtype=np.float32) * np.float32(scale), "fp16")
+    return np.resize(base, shape)
+
+
+def _parallel(items, fn, threads):
+    """fn over items on `threads` Python threads (numpy releases the GIL in BLAS and ufuncs),
+    BLAS limited to one thread each; returns the wall time."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    with _blas_threads(1):
+        t0 = time.perf_counter()
+        with ThreadPoolExecutor(max_workers=threads) as ex:
+            list(ex.map(fn, items))
+        return time.perf_counter() - t0
+
+
+def cpu_swiglu_inputs(rows=512, shape=SWIGLU_SHAPE, cols=None, seed=1):
+    """A row (and optionally column) sample of a swiglu workload for the CPU oracle."""
+    import numpy as np
+
+    M, K, N = shape
+    n = N if cols is None else cols
+    rng = np.random.default_rng(seed)
+    x = _normal_f16(rng, (rows, K))
+    w1 = _normal_f16(rng, (K, n), 1.0 / math.sqrt(K))
+    w3 = _normal_f16(rng, (K, n), 1.0 / math.sqrt(K))
     return x, w1, w3
 
 
-def cpu_swiglu_baseline(inputs=None, min_seconds=8.0, rows=512):
-    """Times the numpy oracle on a bounded row sample of the swiglu workload (all host cores)."""
+def cpu_swiglu_baseline(inputs=None, min_seconds=5.0, rows=512, shape=SWIGLU_SHAPE):
+    """Times the numpy oracle on a bounded sample of a swiglu workload (BLAS on all cores)."""
     from oracle import ops_oracle as O
 
-    M, K, N = SWIGLU_SHAPE
-    x, w1, w3 = inputs if inputs is not None else cpu_swiglu_inputs(rows)
+    M, K, N = shape
+    x, w1, w3 = inputs if inputs is not None else cpu_swiglu_inputs(rows, shape)
     x = x[:rows]
-    O.swiglu(x[:16], w1, w3)  # warm the BLAS thread pool
+    cores = cpu_cores()
+    with _blas_threads(cores):
+        O.swiglu(x[:16], w1, w3)  # warm the BLAS thread pool
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            O.swiglu(x, w1, w3)
+            reps += 1
+            el = time.perf_counter() - t0
+            if (el >= min_seconds and reps >= 2) or reps >= 50:
+                break
+    flops = 4.0 * x.shape[0] * K * w1.shape[1] * reps
+    return {"value": flops / el / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"{reps} x numpy-oracle swiglu on {x.shape[0]} of {M} rows and "
+                      f"{w1.shape[1]} of {N} columns (K={K}), {el:.1f} s; rate extrapolated "
+                      f"to the full workload",
+            "seconds_per_rep": el / reps}
+
+
+def cpu_rmsnorm_baseline(shape=(2, 128, 8, 64), min_seconds=2.0):
+    """The rmsnorm_rope oracle on the full (small) configuration; numpy elementwise work runs
+    on one core."""
+    import numpy as np
+
+    from oracle import ops_oracle as O
+
+    b, s, h, d = shape
+    rng = np.random.default_rng(0)
+    x = _normal_f16(rng, shape)
+    w = O.round_to(1 + 0.1 * rng.standard_normal(d, dtype=np.float32), "fp16")
+    pos = np.arange(s, dtype=np.float32)
+    inv = 1.0 / (10000 ** (np.arange(0, d, 2, dtype=np.float32) / d))
+    emb = np.concatenate([np.outer(pos, inv)] * 2, axis=-1)
+    cos, sin = O.round_to(np.cos(emb), "fp16"), O.round_to(np.sin(emb), "fp16")
+    nbytes = 2 * (b * s * h * d * 2) + d * 2 + 2 * (s * d * 2)
     reps, t0 = 0, time.perf_counter()
     while True:
-        O.swiglu(x, w1, w3)
+        O.rmsnorm_rope(x, w, cos, sin)
         reps += 1
         el = time.perf_counter() - t0
-        if (el >= min_seconds and reps >= 2) or reps >= 50:
+        if el >= min_seconds and reps >= 3:
             break
-    flops = 4.0 * x.shape[0] * K * N * reps
-    return {"value": flops / el / 1e12, "unit": "TFLOP/s", "cores": _cpu_threads(), "kind": "port",
-            "sample": f"{reps} x numpy-oracle swiglu on {x.shape[0]} of {M} rows (K={K}, N={N}), "
-                      f"{el:.1f} s"}
+    return {"value": nbytes * reps / el / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"full configuration {list(shape)}, {reps} calls in {el:.1f} s "
+                      f"(numpy elementwise: one core)"}
 
 
-# ------------------------------------------------------------------------------------------
+def cpu_flash_baseline(b, h, s, d, causal, heads, threads=None):
+    """The flash_attention oracle on `heads` of the b*h heads (one head per thread at a time),
+    rate extrapolated to the whole problem."""
+    import numpy as np
+
+    from oracle import ops_oracle as O
+
+    threads = threads or cpu_cores()
+    rng = np.random.default_rng(2)
+    qkv = [tuple(_normal_f16(rng, (1, 1, s, d)) for _ in range(3)) for _ in range(heads)]
+    el = _parallel(qkv, lambda t: O.flash_attention(*t, causal=causal), min(threads, heads))
+    flops_head = 4.0 * s * s * d * (0.5 if causal else 1.0)
+    return {"value": flops_head * heads / el / 1e12, "unit": "TFLOP/s", "cores": min(threads, heads),
+            "kind": "port",
+            "sample": f"{heads} of {b * h} heads [S={s}, D={d}{', causal' if causal else ''}] in "
+                      f"{el:.1f} s, one head per thread; extrapolated to the full problem"}
+
+
+def cpu_paged_baseline(lens, h, d, bs, threads=None):
+    """The paged_attention oracle on the sequences of `lens` (one sequence per thread at a
+    time), each with its own block pool; GB/s of the algorithmic bytes."""
+    import numpy as np
+
+    from oracle import ops_oracle as O
+
+    threads = threads or cpu_cores()
+    rng = np.random.default_rng(3)
+    cases = []
+    nbytes = 0
+    for n in lens:
+        nb = (n + bs - 1) // bs
+        kc = _normal_f16(rng, (nb, bs, h, d)).astype(np.float16)
+        vc = _normal_f16(rng, (nb, bs, h, d)).astype(np.float16)
+        q = _normal_f16(rng, (1, h, 1, d))
+        bt = np.arange(nb, dtype=np.int32)[None]
+        cases.append((q, kc, vc, bt, np.array([n], np.int32)))
+        nbytes += n * h * d * 2 * 2 + 2 * h * d * 2 + nb * 4 + 4
+    el = _parallel(cases, lambda c: O.paged_attention(*c, block_size=bs), min(threads, len(lens)))
+    return {"value": nbytes / el / 1e9, "unit": "GB/s", "cores": min(threads, len(lens)),
+            "kind": "port",
+            "sample": f"{len(lens)} sequences (lengths {min(lens)}..{max(lens)}, H={h}, D={d}, "
+                      f"block {bs}) in {el:.1f} s, one sequence per thread; extrapolated"}
+
+
 # Single-operator cases (used to profile one kernel at a time from committed code).
 OP_CASES = {
     "swiglu": "swiglu M4096 K4096 N14336 fp16",
@@ -410,89 +539,208 @@ def run_op(args):
                       "unit": unit, "launches": args.steps + args.warmup}), flush=True)
 
 
+def headline_config(world: int, comm: str, chunks: int) -> dict:
+    """The headline workload's config, shared by both arms so the driver sees one config."""
+    M, K, N = SWIGLU_SHAPE
+    return {"workload": f"swiglu M{M} K{K} N{N} fp16 (Llama-3-8B MLP)",
+            "parallelism": "single GPU" if world == 1 else (
+                f"column-shard N over {world} ranks; GEMM epilogue stores every tile into all "
+                f"ranks' [M, N] outputs over NVLink (CUDA IPC), peer handshake inside the kernel"
+                if comm == "peers" else
+                f"column-shard N over {world} ranks + NCCL all_gather_into_tensor + permute "
+                f"into [M, N] ({chunks} row chunk(s))"),
+            "l2": "256 MiB buffer written between timed steps; inputs 267 MB > L2"}
+
+
 def run_reference(args):
+    """CPU arm: the oracle port of the reference's swiglu_ref on the host cores, each step a
+    256-row sample of the headline workload (rate reported; per-step time measured)."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     M, K, N = SWIGLU_SHAPE
-    inputs = cpu_swiglu_inputs(256)
-    vals, cores = [], 1
+    rows = 256
+    inputs = cpu_swiglu_inputs(rows)
+    vals, secs, cores = [], [], cpu_cores()
     for i in range(args.warmup + args.steps):
-        b = cpu_swiglu_baseline(inputs, min_seconds=0.0, rows=256)
-        cores = b["cores"]
+        b = cpu_swiglu_baseline(inputs, min_seconds=0.0, rows=rows)
         if i >= args.warmup:
             vals.append(b["value"])
+            secs.append(b["seconds_per_rep"])
     v = statistics.median(vals)
-    ms = 4.0 * M * K * N / (v * 1e12) * 1e3
+    ms = statistics.median(secs) * 1e3
     line = {
         "impl": "reference", "metric": "swiglu TFLOP/s", "value": v, "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
         "data": "synthetic (seeded normal, x~N(0,1), w~N(0,1/K))",
-        "config": {"workload": f"swiglu M{M} K{K} N{N} fp16 (Llama-3-8B MLP)",
-                   "note": "CPU oracle (numpy restatement of reference/swiglu.py); each step is a "
-                           "256-row sample, extrapolated to the full workload"},
+        "config": headline_config(world, args.comm, args.chunks),
+        "note": (f"CPU oracle (numpy restatement of reference/swiglu.py) on {cores} host threads; "
+                 f"each step is one {rows}-row sample of the workload ({ms:.0f} ms measured); value "
+                 f"is the sample's rate; the full workload would take "
+                 f"{4.0 * M * K * N / (v * 1e12) * 1e3:.0f} ms per step at that rate"),
         "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                         "sample": "256-row samples of the swiglu workload per step"},
+                         "sample": f"{rows}-row samples of the swiglu workload, one per step"},
         "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 # ------------------------------------------------------------------------------------------
-def extra_ops(torch, T, peaks):
-    """The other three operators at their configurations (N=1, rank 0)."""
+def _median_ms(torch, fn, steps, warmup, flush=None):
+    return statistics.median(_events_time(torch, fn, steps, warmup, flush))
+
+
+def _e2e(torch, pairs, run, out_host, steps=3, warmup=2, note=""):
+    """End to end through the public operator: each step copies every (pinned host, device)
+    input pair host -> device, runs the operator and copies its result into the pinned host
+    buffer, all on the current stream; CUDA events around the whole step."""
+    def step():
+        for h, d in pairs:
+            d.copy_(h, non_blocking=True)
+        out_host.copy_(run(), non_blocking=True)
+
+    ms = _median_ms(torch, step, steps, warmup)
+    h2d = sum(h.numel() * h.element_size() for h, _ in pairs)
+    d2h = out_host.numel() * out_host.element_size()
+    return {"ms": ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "path": note or "H2D copies from pinned host memory, the public operator, D2H copy; one stream"}
+
+
+def _pinned_like(torch, t):
+    h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+    h.copy_(t)
+    return h
+
+
+def _roofline(achieved, peak, unit, bound, peak_src, traffic=None, kernel=None, note=None):
+    r = {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+         "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src}
+    if kernel:
+        r["kernel"] = kernel
+    if note:
+        r["note"] = note
+    return r
+
+
+def _paged_meta(batch, seed=3, lo=512, hi=8192, h=32, d=128, bs=16):
+    """Lengths and algorithmic bytes of the seeded paged decode case (no device memory)."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(lo, hi + 1, (batch,), dtype=torch.int32, generator=g)
+    nb = [(int(n) + bs - 1) // bs for n in lens]
+    nbytes = int(lens.sum()) * h * d * 2 * 2 + 2 * batch * h * d * 2 + sum(nb) * 4 + batch * 4
+    return [int(n) for n in lens], nbytes
+
+
+# ------------------------------------------------------------------------------------------
+def extra_ops(torch, T, peaks, peak_src, with_cpu=True):
+    """The other three operators at their configurations and the extensions (N=1, rank 0)."""
     res = {}
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     hbm = peaks["hbm_gbs"]
     tc = peaks["bf16_tflops"]
+    hbm_src = f"{peak_src} hbm_gbs (copy)"
+    tc_src = f"{peak_src} bf16_tflops (dense, burst)"
 
     def gen(shape, seed, scale=1.0):
         g = torch.Generator(device="cuda").manual_seed(seed)
         return (torch.randn(shape, generator=g, device="cuda") * scale).half()
+
+    def rope_tables(s, d):
+        pos = torch.arange(s, device="cuda", dtype=torch.float32)
+        inv = 1.0 / (10000 ** (torch.arange(0, d, 2, device="cuda").float() / d))
+        emb = torch.cat([torch.outer(pos, inv)] * 2, dim=-1)
+        return emb.cos().half(), emb.sin().half()
 
     # rmsnorm_rope: config [2,128,8,64] and a bandwidth-scale variant [16,4096,32,128].
     for name, (b, s, h, d) in [("rmsnorm_rope_cfg_2x128x8x64", (2, 128, 8, 64)),
                                ("rmsnorm_rope_bw_16x4096x32x128", (16, 4096, 32, 128))]:
         x = gen((b, s, h, d), 0)
         w = (1 + 0.1 * torch.randn(d, device="cuda")).half()
-        pos = torch.arange(s, device="cuda", dtype=torch.float32)
-        inv = 1.0 / (10000 ** (torch.arange(0, d, 2, device="cuda").float() / d))
-        emb = torch.cat([torch.outer(pos, inv)] * 2, dim=-1)
-        cos, sin = emb.cos().half(), emb.sin().half()
+        cos, sin = rope_tables(s, d)
         nbytes = 2 * (b * s * h * d * 2) + d * 2 + 2 * (s * d * 2)
+        fn = lambda: T.rmsnorm_rope(x, w, cos, sin)  # noqa: E731
         with ClockSampler(torch.cuda.current_device()) as clk:
-            ts = _events_time(torch, lambda: T.rmsnorm_rope(x, w, cos, sin), 20, 5, flush)
-        t = statistics.median(ts)
+            t = _median_ms(torch, fn, 20, 5, flush)
         gbs = nbytes / (t * 1e-3) / 1e9
-        res[name] = {"value": gbs, "unit": "GB/s", "ms": t, "bytes": nbytes,
-                     "roofline_frac": gbs / hbm, "bound": "hbm", "l2": "flushed",
-                     "sm_mhz": clk.summary().get("sm_mhz")}
+        cfg = b == 2
+        traffic = None if cfg else profile_traffic("rmsnorm_rope_vec_kernel_16x4096x32x128_fp16.md")
+        ent = {"value": gbs, "unit": "GB/s", "ms": t, "bytes": nbytes, "roofline_frac": gbs / hbm,
+               "bound": "hbm", "l2": "flushed", "sm_mhz": clk.summary().get("sm_mhz"),
+               "roofline": _roofline(gbs, hbm, "GB/s", "hbm", hbm_src, traffic,
+                                     "rmsnorm_rope_vec_kernel")}
+        if cfg:
+            hx, hw, hc, hs = (_pinned_like(torch, t_) for t_ in (x, w, cos, sin))
+            hout = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+            dx, dw, dc, ds = (torch.empty_like(t_) for t_ in (x, w, cos, sin))
+            e = _e2e(torch, [(hx, dx), (hw, dw), (hc, dc), (hs, ds)],
+                     lambda: T.rmsnorm_rope(dx, dw, dc, ds), hout, steps=20, warmup=5)
+            e.update(value=nbytes / (e["ms"] * 1e-3) / 1e9, unit="GB/s")
+            ent["e2e"] = e
+            if with_cpu:
+                ent["cpu_baseline"] = cpu_rmsnorm_baseline((b, s, h, d))
+        res[name] = ent
         del x
     # flash_attention: causal [4,32,4096,128] and non-causal [4,32,1024,128].
-    for name, (b, h, s, d), causal in [("flash_causal_4x32x4096x128", (4, 32, 4096, 128), True),
-                                       ("flash_full_4x32x1024x128", (4, 32, 1024, 128), False)]:
+    for name, (b, h, s, d), causal, cpu_heads in [
+            ("flash_causal_4x32x4096x128", (4, 32, 4096, 128), True, 8),
+            ("flash_full_4x32x1024x128", (4, 32, 1024, 128), False, 32)]:
         q, k, v = gen((b, h, s, d), 2), gen((b, h, s, d), 3), gen((b, h, s, d), 4)
         flops = 4.0 * b * h * s * s * d * (0.5 if causal else 1.0)
         with ClockSampler(torch.cuda.current_device()) as clk:
-            ts = _events_time(torch, lambda: T.flash_attention(q, k, v, causal=causal), 10, 3, flush)
-        t = statistics.median(ts)
+            t = _median_ms(torch, lambda: T.flash_attention(q, k, v, causal=causal), 10, 3, flush)
         tf = flops / (t * 1e-3) / 1e12
-        res[name] = {"value": tf, "unit": "TFLOP/s", "ms": t, "flops": flops,
-                     "roofline_frac": tf / tc, "bound": "tensor",
-                     "sm_mhz": clk.summary().get("sm_mhz")}
-        del q, k, v
+        traffic = profile_traffic("flash_pp_kernel_causal_b4_h32_s4096_d128_fp16.md") if causal else None
+        ent = {"value": tf, "unit": "TFLOP/s", "ms": t, "flops": flops, "roofline_frac": tf / tc,
+               "bound": "tensor", "sm_mhz": clk.summary().get("sm_mhz"),
+               "roofline": _roofline(tf, tc, "TFLOP/s", "tensor", tc_src, traffic, "flash_pp_kernel")}
+        hq, hk, hv = (_pinned_like(torch, t_) for t_ in (q, k, v))
+        hout = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+        dq, dk, dv = (torch.empty_like(t_) for t_ in (q, k, v))
+        e = _e2e(torch, [(hq, dq), (hk, dk), (hv, dv)],
+                 lambda: T.flash_attention(dq, dk, dv, causal=causal), hout)
+        e.update(value=flops / (e["ms"] * 1e-3) / 1e12, unit="TFLOP/s")
+        ent["e2e"] = e
+        if with_cpu:
+            ent["cpu_baseline"] = cpu_flash_baseline(b, h, s, d, causal, cpu_heads)
+        res[name] = ent
+        del q, k, v, dq, dk, dv, hq, hk, hv, hout
     # paged_attention decode: B64 H32 D128 bs16, lens U[512,8192] (seed 3).
     qd, kc, vc, btd, cl, nbytes = _paged_inputs(torch, 64)
+    fn = lambda: T.paged_attention(qd, kc, vc, btd, cl, block_size=16)  # noqa: E731
     with ClockSampler(torch.cuda.current_device()) as clk:
-        ts = _events_time(torch, lambda: T.paged_attention(qd, kc, vc, btd, cl, block_size=16), 20, 5, flush)
-    t = statistics.median(ts)
+        t = _median_ms(torch, fn, 20, 5, flush)
     gbs = nbytes / (t * 1e-3) / 1e9
-    res["paged_decode_b64_h32_d128_bs16"] = {"value": gbs, "unit": "GB/s", "ms": t, "bytes": nbytes,
-                                              "roofline_frac": gbs / hbm, "bound": "hbm",
-                                              "kv_tokens": int(cl.sum().item()),
-                                              "sm_mhz": clk.summary().get("sm_mhz")}
-    del kc, vc
+    tr16 = profile_traffic("paged_split_kernel_b16_h32_d128_bs16_fp16.md")
+    traffic = tr16 * nbytes / _paged_meta(16)[1] if tr16 else None
+    ent = {"value": gbs, "unit": "GB/s", "ms": t, "bytes": nbytes, "roofline_frac": gbs / hbm,
+           "bound": "hbm", "kv_tokens": int(cl.sum().item()), "sm_mhz": clk.summary().get("sm_mhz"),
+           "roofline": _roofline(gbs, hbm, "GB/s", "hbm", hbm_src, traffic, "paged_split_kernel",
+                                 "traffic: the B16 capture scaled to B64 by algorithmic bytes")}
+    hq, hk, hv, hb, hl = (_pinned_like(torch, t_) for t_ in (qd, kc, vc, btd, cl))
+    hout = torch.empty(qd.shape, dtype=qd.dtype, pin_memory=True)
+    dq, dk, dv, db, dl = (torch.empty_like(t_) for t_ in (qd, kc, vc, btd, cl))
+    e = _e2e(torch, [(hq, dq), (hk, dk), (hv, dv), (hb, db), (hl, dl)],
+             lambda: T.paged_attention(dq, dk, dv, db, dl, block_size=16), hout,
+             note="every input (the 4.3 GB KV cache included) copied from pinned host memory, "
+                  "the operator, the result copied back; one stream")
+    e.update(value=nbytes / (e["ms"] * 1e-3) / 1e9, unit="GB/s")
+    del dk, dv
+    er = _e2e(torch, [(hq, dq), (hb, db), (hl, dl)],
+              lambda: T.paged_attention(dq, kc, vc, db, dl, block_size=16), hout, steps=10,
+              note="KV cache resident in HBM (as a serving engine holds it); q, block tables and "
+                   "lengths copied in and the result out every step")
+    er.update(value=nbytes / (er["ms"] * 1e-3) / 1e9, unit="GB/s")
+    e["cache_resident"] = er
+    ent["e2e"] = e
+    if with_cpu:
+        lens64, _ = _paged_meta(64)
+        ent["cpu_baseline"] = cpu_paged_baseline(lens64[:8], 32, 128, 16)
+    res["paged_decode_b64_h32_d128_bs16"] = ent
+    del kc, vc, hk, hv
     torch.cuda.empty_cache()
     # Operators either side of decode (extensions of the reference's set): GQA decode with 1
     # and 4 new tokens per sequence and a causal prefill chunk through the paged cache, and
@@ -600,11 +848,201 @@ def extra_ops(torch, T, peaks):
     return res
 
 
+# ------------------------------------------------------------------------------------------
+def _max_over_ranks(torch, dist, world, v):
+    if world == 1:
+        return v
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _sum_over_ranks(torch, dist, world, v: int) -> int:
+    if world == 1:
+        return int(v)
+    t = torch.tensor([int(v)], device="cuda", dtype=torch.int64)
+    dist.all_reduce(t)
+    return int(t.item())
+
+
+def _all_ok(torch, dist, world, ok: bool) -> bool:
+    if world == 1:
+        return bool(ok)
+    t = torch.tensor([1 if ok else 0], device="cuda", dtype=torch.int32)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item())
+
+
+def _bits_checksum(torch, t) -> int:
+    """Exact checksum of a 16-bit tensor: the sum of its bit patterns (order-independent)."""
+    flat = t.reshape(-1).view(torch.int16)
+    total = 0
+    step = 1 << 26
+    for i in range(0, flat.numel(), step):
+        total += int(flat[i:i + step].to(torch.int64).sum().item())
+    return total
+
+
+def _timed_ranks(torch, dist, world, fn, steps, warmup, flush=None):
+    """Median per-step device time of fn on this rank, then the max over ranks."""
+    fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = _median_ms(torch, fn, steps, warmup, flush)
+    return _max_over_ranks(torch, dist, world, ms)
+
+
+def sharded_cfg5(torch, dist, T, S, world, rank, local, peaks, peak_src, with_cpu):
+    """The Llama-3-70B-shaped sharded workloads at this world size (every rank)."""
+    res = {}
+    tc = peaks["bf16_tflops"]
+    hbm = peaks["hbm_gbs"]
+    dev = torch.device("cuda", local)
+
+    # swiglu: x [8192, 8192], w1/w3 [8192, 28672] column-sharded, output gathered on every rank.
+    M, K, N = CFG5_SWIGLU
+    n_loc = N // world
+    g = torch.Generator(device="cuda").manual_seed(4)
+    x = torch.randn(M, K, generator=g, device="cuda").half()
+    w1 = (torch.randn(K, N, generator=g, device="cuda") / math.sqrt(K)).half()
+    w3 = (torch.randn(K, N, generator=g, device="cuda") / math.sqrt(K)).half()
+    r0, r1 = 4096, 4352
+    ref_rows = T.swiglu(x[r0:r1].contiguous(), w1, w3)
+    w1l = w1[:, rank * n_loc:(rank + 1) * n_loc].contiguous()
+    w3l = w3[:, rank * n_loc:(rank + 1) * n_loc].contiguous()
+    del w1, w3
+    torch.cuda.empty_cache()
+    peers = None
+    if world > 1:
+        peers = S.PeerBuffers((M, N), torch.float16, dev)
+        step = lambda: S.swiglu_column_sharded(x, w1l, w3l, peers=peers)  # noqa: E731
+    else:
+        step = lambda: T.swiglu(x, w1l, w3l)  # noqa: E731
+    ms = _timed_ranks(torch, dist, world, step, 5, 2)
+    out = step()
+    torch.cuda.synchronize()
+    ok = _all_ok(torch, dist, world, bool(torch.equal(out[r0:r1], ref_rows)))
+    flops = 4.0 * M * K * N
+    tf = flops / (ms * 1e-3) / 1e12
+    t_tc = 4.0 * M * K * n_loc / (tc * 1e12)
+    t_link = (world - 1) * M * n_loc * 2 / (NVLINK_GBS * 1e9) if world > 1 else 0.0
+    ent = {"value": tf, "unit": "TFLOP/s", "ms": ms, "flops": flops,
+           "per_rank": f"x [{M}, {K}] and w1/w3 column slices [{K}, {n_loc}]; every rank ends "
+                       f"with the whole [{M}, {N}] output",
+           "parity": {"ok": ok, "check": f"rows {r0}:{r1} of every rank's gathered output equal "
+                                         f"bit for bit the single-GPU swiglu of those rows"},
+           "roofline": {"bound": "tensor" if t_tc >= t_link else "nvlink",
+                        "target_ms": max(t_tc, t_link) * 1e3, "tensor_ms": t_tc * 1e3,
+                        "nvlink_ms": t_link * 1e3, "frac": max(t_tc, t_link) * 1e3 / ms,
+                        "note": f"slower of local FLOPs / {peak_src} bf16 peak {tc:.0f} TFLOP/s and "
+                                f"bytes sent per rank / {NVLINK_GBS:.0f} GB/s peer-copy rate"}}
+    if world > 1:
+        ent["nvlink_gbs_per_rank"] = (world - 1) * M * n_loc * 2 / (ms * 1e-3) / 1e9
+    if with_cpu:
+        ent["cpu_baseline"] = cpu_swiglu_baseline(cpu_swiglu_inputs(256, CFG5_SWIGLU, cols=4096, seed=4),
+                                                  min_seconds=3.0, rows=256, shape=CFG5_SWIGLU)
+    res["swiglu_m8192_k8192_n28672"] = ent
+    if peers is not None:
+        torch.cuda.synchronize()
+        dist.barrier()
+        peers.close()
+    del x, w1l, w3l, ref_rows, out, peers
+    torch.cuda.empty_cache()
+
+    # flash_attention causal [8, 64, 8192, 128], heads sharded.
+    B, H, Sq, D = CFG5_FLASH
+    h0, h1 = S.head_range(H, rank, world)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    loc = []
+    for _ in range(3):
+        full = torch.randn(B, H, Sq, D, generator=g, device="cuda").half()
+        loc.append(full[:, h0:h1].contiguous())
+        del full
+        torch.cuda.empty_cache()
+    q, k, v = loc
+    fn = lambda: S.flash_attention_head_sharded(q, k, v, causal=True)  # noqa: E731
+    ms = _timed_ranks(torch, dist, world, fn, 5, 2)
+    out = fn()
+    torch.cuda.synchronize()
+    chk = _sum_over_ranks(torch, dist, world, _bits_checksum(torch, out))
+    flops = 4.0 * B * H * Sq * Sq * D * 0.5
+    tf = flops / (ms * 1e-3) / 1e12
+    ent = {"value": tf, "unit": "TFLOP/s", "ms": ms, "flops": flops,
+           "per_rank": f"heads [{h0}, {h1}) of q/k/v/o, no communication",
+           "checksum_fp16_bits": chk,
+           "roofline": _roofline(tf / world, tc, "TFLOP/s", "tensor", f"{peak_src} bf16_tflops",
+                                 kernel="flash_pp_kernel", note="achieved per GPU")}
+    if with_cpu:
+        ent["cpu_baseline"] = cpu_flash_baseline(B, H, Sq, D, True, 4, threads=4)
+    res["flash_causal_b8_h64_s8192_d128"] = ent
+    del q, k, v, out, loc
+    torch.cuda.empty_cache()
+
+    # paged decode B256 H64 D128 bs32, lens U[1024, 32768], sequences balanced by tokens.
+    Bp, Hp, Dp, bs, lo, hi = CFG5_PAGED
+    gc = torch.Generator().manual_seed(4)
+    lens = torch.randint(lo, hi + 1, (Bp,), dtype=torch.int32, generator=gc)
+    nb = [(int(n) + bs - 1) // bs for n in lens]
+    pool = sum(nb)
+    perm = torch.randperm(pool, generator=gc)
+    bt = torch.zeros(Bp, max(nb), dtype=torch.int32)
+    pos = 0
+    for i, n in enumerate(nb):
+        bt[i, :n] = perm[pos:pos + n].to(torch.int32)
+        pos += n
+    parts = S.partition_sequences(lens.tolist(), world, "tokens")
+    counts = S.partition_sequences(lens.tolist(), world, "count")
+    toks = [sum(int(lens[i]) for i in p) for p in parts]
+    toks_c = [sum(int(lens[i]) for i in p) for p in counts]
+    seqs = parts[rank]
+    ids, lbt, llen = S.localize_blocks(bt, lens, seqs, bs)
+    # Physical block p of the global pool holds reservoir block p % R (seeded, identical on
+    # every rank), so each rank builds only its own blocks and the values do not depend on
+    # the world size.
+    R = 2053
+    gd = torch.Generator(device="cuda").manual_seed(4)
+    res_k = torch.randn(R, bs, Hp, Dp, generator=gd, device="cuda").half()
+    res_v = torch.randn(R, bs, Hp, Dp, generator=gd, device="cuda").half()
+    q_all = torch.randn(Bp, Hp, 1, Dp, generator=gd, device="cuda").half()
+    sel = (ids % R).cuda()
+    kc = res_k.index_select(0, sel)
+    vc = res_v.index_select(0, sel)
+    del res_k, res_v, sel
+    torch.cuda.empty_cache()
+    qs = q_all[torch.tensor(seqs, dtype=torch.int64, device="cuda")].contiguous()
+    lbt_d, llen_d = lbt.cuda(), llen.cuda()
+    fn = lambda: T.paged_attention(qs, kc, vc, lbt_d, llen_d, block_size=bs)  # noqa: E731
+    ms = _timed_ranks(torch, dist, world, fn, 5, 2)
+    out = fn()
+    torch.cuda.synchronize()
+    chk = _sum_over_ranks(torch, dist, world, _bits_checksum(torch, out))
+    nbytes = int(lens.sum()) * Hp * Dp * 2 * 2 + 2 * Bp * Hp * Dp * 2 + pool * 4 + Bp * 4
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    mean = sum(toks) / world
+    ent = {"value": gbs, "unit": "GB/s", "ms": ms, "bytes": nbytes, "kv_tokens": int(lens.sum()),
+           "per_rank": f"{len(seqs)} whole sequences ({toks[rank]} tokens), their block-table rows "
+                       f"and a rank-local pool of their {len(ids)} blocks; no communication",
+           "balance": {"tokens_scheme_max_over_mean": max(toks) / mean,
+                       "count_scheme_max_over_mean": max(toks_c) / mean},
+           "checksum_fp16_bits": chk,
+           "roofline": _roofline(gbs / world, hbm, "GB/s", "hbm", f"{peak_src} hbm_gbs",
+                                 kernel="paged_split_kernel + paged_merge_kernel",
+                                 note="achieved per GPU")}
+    if with_cpu:
+        ent["cpu_baseline"] = cpu_paged_baseline([int(n) for n in lens[:2]], Hp, Dp, bs, threads=2)
+    res["paged_decode_b256_h64_d128_bs32"] = ent
+    del kc, vc, q_all, qs, out
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
 
     import tritonllmcompiler_b200 as T
+    from tritonllmcompiler_b200 import sharded as S
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -621,15 +1059,12 @@ def run_ours(args):
     x = torch.randn(M, K, generator=g, device="cuda").half()
     w1 = (torch.randn(K, N, generator=g, device="cuda") / math.sqrt(K)).half()
     w3 = (torch.randn(K, N, generator=g, device="cuda") / math.sqrt(K)).half()
+    r0, r1 = PARITY_ROWS
+    ref_rows = T.swiglu(x[r0:r1].contiguous(), w1, w3)  # parity reference: the rows alone
     w1l = w1[:, rank * n_loc:(rank + 1) * n_loc].contiguous()
     w3l = w3[:, rank * n_loc:(rank + 1) * n_loc].contiguous()
     del w1, w3
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
-
-    def kernel_only():
-        return T.swiglu(x, w1l, w3l)
-
-    from tritonllmcompiler_b200 import sharded as S
 
     out_full = None
     peers = None
@@ -647,7 +1082,6 @@ def run_ours(args):
         return S.swiglu_column_sharded(x, w1l, w3l, chunks=args.chunks, out=out_full)
 
     flops = 4.0 * M * K * N
-    # Warm-up (also JIT-free: the library is prebuilt).
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -657,34 +1091,61 @@ def run_ours(args):
     with ClockSampler(local) as clk:
         times = _events_time(torch, step, args.steps, 0, flush)
     torch.cuda.synchronize()
-    t_step = sum(times) / len(times)
+    t_step = _max_over_ranks(torch, dist, world, sum(times) / len(times))
     if world > 1:
-        tt = torch.tensor([t_step], device="cuda")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_step = float(tt.item())
         dist.barrier()
     value = flops / (t_step * 1e-3) / 1e12
 
-    # Kernel-only roofline: the swiglu kernel alone, CUDA events on its launch stream.
-    kt = _events_time(torch, kernel_only, max(5, args.steps // 2), 2, flush)
-    k_ms = sum(kt) / len(kt)
-    k_flops = 4.0 * M * K * n_loc
-    achieved = k_flops / (k_ms * 1e-3) / 1e12
-    traffic = profile_traffic("swiglu_pair_kernel_m4096_k4096_n14336_fp16.md") if world == 1 else None
+    # Parity: the sampled rows of the (gathered) output against the rows computed alone.
+    out = step()
+    torch.cuda.synchronize()
+    parity_ok = _all_ok(torch, dist, world, bool(torch.equal(out[r0:r1], ref_rows)))
+    del out
+
+    # Roofline of the kernel that runs in the step. One GPU (or the NCCL path): the swiglu
+    # kernel alone on the local shard. Peer stores: the step is that one kernel.
+    peak = peaks["bf16_tflops"]
+    if world == 1 or peers is None:
+        k_ms = _max_over_ranks(torch, dist, world,
+                               _median_ms(torch, lambda: T.swiglu(x, w1l, w3l), max(5, args.steps // 2), 2, flush))
+        achieved = 4.0 * M * K * n_loc / (k_ms * 1e-3) / 1e12
+        roofline = _roofline(achieved, peak, "TFLOP/s", "tensor", f"{peak_src} bf16_tflops (dense, burst)",
+                             profile_traffic("swiglu_pair_kernel_m4096_k4096_n14336_fp16.md") if world == 1 else None,
+                             "swiglu_pair_kernel" + ("" if world == 1 else " (local shard, local output)"))
+        roofline["kernel_ms"] = k_ms
+    else:
+        k_ms = t_step
+        t_tc = 4.0 * M * K * n_loc / (peak * 1e12)
+        sent = (world - 1) * M * n_loc * 2
+        t_link = sent / (NVLINK_GBS * 1e9)
+        if t_tc >= t_link:
+            roofline = _roofline(4.0 * M * K * n_loc / (k_ms * 1e-3) / 1e12, peak, "TFLOP/s", "tensor",
+                                 f"{peak_src} bf16_tflops (dense, burst)", None,
+                                 "swiglu_pair_kernel<peers> (GEMM + output all-gather over NVLink)")
+        else:
+            roofline = _roofline(sent / (k_ms * 1e-3) / 1e9, NVLINK_GBS, "GB/s", "nvlink",
+                                 "measured NVLink peer-copy rate per direction on this pool", None,
+                                 "swiglu_pair_kernel<peers> (GEMM + output all-gather over NVLink)")
+        roofline.update(kernel_ms=k_ms, tensor_ms=t_tc * 1e3, nvlink_ms=t_link * 1e3,
+                        bytes_sent_per_rank=sent,
+                        local_tflops=4.0 * M * K * n_loc / (k_ms * 1e-3) / 1e12,
+                        note="the step is this one kernel; its target is the slower of local FLOPs / "
+                             "bf16 peak and bytes sent per rank / NVLink rate")
+        traffic = profile_traffic(f"swiglu_pair_kernel_peers_m4096_k4096_n14336_g{world}.md")
+        roofline["traffic"] = traffic
 
     # End to end through the public API with pinned host buffers (H2D inputs, D2H result).
     hx = x.cpu().pin_memory()
     h1 = w1l.cpu().pin_memory()
     h3 = w3l.cpu().pin_memory()
-    hout = torch.empty((M, n_loc), dtype=torch.float16).pin_memory()
     dx, d1, d3 = torch.empty_like(x), torch.empty_like(w1l), torch.empty_like(w3l)
-
     if world > 1:
         hout = torch.empty((M, N), dtype=torch.float16).pin_memory()
     else:
         # One GPU: the public host-memory entry, which pipelines the weight upload, the kernel
         # and the result download over column blocks on three streams.
         from tritonllmcompiler_b200.ops.host_pipeline import SwigluHostPipeline
+        hout = torch.empty((M, n_loc), dtype=torch.float16).pin_memory()
         host_pipe = SwigluHostPipeline(M, n_loc, K, torch.float16, torch.device("cuda", local),
                                        chunks=args.e2e_chunks)
 
@@ -701,50 +1162,49 @@ def run_ours(args):
             out = S.swiglu_column_sharded(dx, d1, d3, chunks=args.chunks, out=out_full)
         hout.copy_(out, non_blocking=True)
 
-    et = _events_time(torch, e2e_step, max(3, args.steps // 4), 2)
-    e_ms = sum(et) / len(et)
-    if world > 1:
-        tt = torch.tensor([e_ms], device="cuda")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e_ms = float(tt.item())
+    e_ms = _max_over_ranks(torch, dist, world,
+                           sum(_events_time(torch, e2e_step, max(3, args.steps // 4), 2)) / max(3, args.steps // 4))
     e2e = {"value": flops / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
            "h2d_bytes_per_step": (hx.numel() + h1.numel() + h3.numel()) * 2,
            "d2h_bytes_per_step": hout.numel() * 2, "ms_per_step": e_ms,
            "path": (f"ops.host_pipeline.SwigluHostPipeline, {len(host_pipe.blocks)} column blocks: "
                     f"upload, kernel and download overlapped on three streams") if world == 1 else
-                   "H2D copies, sharded swiglu, D2H copy on one stream"}
+                   "per rank: H2D copies of x and its weight slices, sharded swiglu, D2H copy of the "
+                   "whole [M, N] output; one stream"}
+    del dx, d1, d3, hx, h1, h3, hout, x, w1l, w3l, flush
+    if world == 1:
+        del host_pipe
+    if peers is not None:
+        torch.cuda.synchronize()
+        dist.barrier()
+        peers.close()
+        peers = None
+    out_full = None
+    torch.cuda.empty_cache()
 
     ops = None
     cpu = None
     if rank == 0 and world == 1:
         if not args.no_ops:
-            del dx, d1, d3, host_pipe
-            torch.cuda.empty_cache()
-            ops = extra_ops(torch, T, peaks)
+            ops = extra_ops(torch, T, peaks, peak_src, with_cpu=not args.no_cpu)
         if not args.no_cpu:
             cpu = cpu_swiglu_baseline()
+    cfg5 = None
+    if not args.no_cfg5:
+        cfg5 = sharded_cfg5(torch, dist, T, S, world, rank, local, peaks, peak_src,
+                            with_cpu=(rank == 0 and world == 1 and not args.no_cpu))
 
     if rank == 0:
-        peak = peaks["bf16_tflops"]
         line = {
             "metric": "swiglu TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic (seeded normal, x~N(0,1), w~N(0,1/K))",
-            "config": {"workload": f"swiglu M{M} K{K} N{N} fp16 (Llama-3-8B MLP)",
-                       "parallelism": "single GPU" if world == 1 else (
-                           f"column-shard N over {world} ranks; GEMM epilogue stores every "
-                           f"tile into all ranks' [M, N] outputs over NVLink (CUDA IPC)"
-                           if args.comm == "peers" else
-                           f"column-shard N over {world} ranks + NCCL all_gather_into_tensor + "
-                           f"permute into [M, N] ({args.chunks} row chunk(s))"),
-                       "l2": "256 MiB buffer written between timed steps; inputs 267 MB > L2"},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": traffic,
-                         "peak_source": f"{peak_src} bf16_tflops (dense, burst)",
-                         "kernel_ms": k_ms,
-                         "kernel": ("swiglu_pair_kernel" if world == 1 or args.comm != "peers"
-                                    else "swiglu_tc_kernel (column-sharded, peer stores)")},
+            "config": headline_config(world, args.comm, args.chunks),
+            "parity": {"ok": parity_ok,
+                       "check": f"rows {r0}:{r1} of the step's [M, N] output on every rank equal, bit "
+                                f"for bit, swiglu of those rows computed alone on one GPU"},
+            "roofline": roofline,
             "e2e": e2e,
             "gpu_launches": args.steps,
             "clocks": clk.summary(),
@@ -752,12 +1212,17 @@ def run_ours(args):
         }
         if ops is not None:
             line["ops"] = ops
+        if cfg5 is not None:
+            line["sharded_cfg5"] = cfg5
+            line["sharded_cfg5_note"] = (
+                "Llama-3-70B-shaped workloads sharded over the ranks of this run; value is the "
+                "whole-job rate from the max-over-ranks device time (median of 5 steps after 2 "
+                "warm-up); inputs larger than L2; the checksums are exact sums of the output's "
+                "fp16 bit patterns, equal at every world size when the sharded result matches "
+                "the single-GPU one")
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.cuda.synchronize()
-        dist.barrier()
-        if peers is not None:
-            peers.close()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -186,6 +186,37 @@ TLLM_API int tllm_swiglu_colshard(const void *x, const void *w1, const void *w3,
                                   int64_t N, int64_t K, int64_t lda, int64_t ldb1, int64_t ldb3,
                                   int64_t ldo, int dtype, void *stream);
 
+/* Flag words per rank of tllm_swiglu_colshard_peers (uint32, zero before the first call). */
+#define TLLM_SWIGLU_PEER_FLAG_WORDS 16
+
+/*
+ * Column-sharded SwiGLU whose output all-gather and its synchronisation both live in the
+ * kernel (no counterpart in the reference, which is single-GPU). Rank `rank` of `ndst`
+ * (one process per GPU of one node) computes silu(x @ w1) * (x @ w3) for its column slices
+ * w1/w3 [K, N] and stores the [M, N] result at column offset rank * N of every rank's
+ * [M, ndst * N] output dsts[0..ndst) (row stride ldo; the peers' buffers mapped into this
+ * process with tllm_ipc_open) over NVLink, tile by tile as the GEMM finishes them.
+ *   flags[d]: rank d's TLLM_SWIGLU_PEER_FLAG_WORDS words (mapped likewise), zeroed before
+ *     the first call; done: one uint32 of this rank's device memory, zeroed likewise; epoch:
+ *     1 on the first call with these buffers, +1 on every later one, the same on every rank.
+ *   At its start a launch tells every peer it has begun (its stream's earlier work, reads of
+ *   the previous output included, is complete); a CTA stores into a peer only once that
+ *   peer has begun; the launch ends only after every peer has reported its stores into this
+ *   rank complete. No host-side barrier is needed between calls, and a call's output is
+ *   complete when the launch ends on this rank's stream. Every rank must make every call.
+ *   Waits are bounded (about 2 s); a peer that never starts or finishes is reported through
+ *   tllm_debug_status (TLLM_DEV_WAIT_TIMEOUT + 5 or + 6) instead of hanging.
+ *   variant: 0 automatic (the CTA-pair kernel with tensor stores from M >= 256 when N % 128
+ *   == 0 and ldo, N and the buffers allow 16-byte-aligned slices), 1 the one-CTA kernel,
+ *   2 the CTA-pair kernel. ndst <= 8; K, N and the leading dimensions multiples of 8.
+ */
+TLLM_API int tllm_swiglu_colshard_peers(const void *x, const void *w1, const void *w3,
+                                        void *const *dsts, uint32_t *const *flags, int ndst,
+                                        int rank, uint32_t *done, uint32_t epoch, int64_t M,
+                                        int64_t N, int64_t K, int64_t lda, int64_t ldb1,
+                                        int64_t ldb3, int64_t ldo, int dtype, int variant,
+                                        void *stream);
+
 /* CUDA IPC set-up helpers for tllm_swiglu_colshard's peer buffers: a 64-byte handle and
  * byte offset for a device pointer, opening a peer's handle in this process, and closing it.
  * Not on the hot path. */

@@ -24,6 +24,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <cstring>
+
 #include "common.h"
 #include "ptx.cuh"
 
@@ -68,6 +70,8 @@ enum : int {
   SITE_FULL = 2,
   SITE_TEMPTY = 3,
   SITE_TFULL = 4,
+  SITE_PEER_READY = 5,   // a peer's call did not start
+  SITE_PEER_ARRIVE = 6,  // a peer's stores did not complete
 };
 
 constexpr int kMaxDst = 8;
@@ -84,7 +88,73 @@ struct Geom {
   int ndst;
   int64_t col_off;
   void *dst[kMaxDst];
+  // Peer handshake of the column-sharded mode (flags[0] == nullptr: none, the caller orders
+  // the calls). flags[d] points at rank d's flag words as mapped into this process: words
+  // [kFlagReady + s] and [kFlagArrive + s] are written by rank s. rank is this rank's index
+  // among the destinations, done counts this launch's finished CTAs (zero between launches),
+  // epoch numbers the call (1, 2, ... per set of buffers).
+  uint32_t *flags[kMaxDst];
+  int rank;
+  uint32_t *done;
+  uint32_t epoch;
 };
+
+// Tensor maps of the destinations' column slices (column-sharded CTA-pair kernel): map d
+// covers [M, N] at column offset col_off of destination d, boxes of 64 columns x 32 rows,
+// 128-byte swizzle.
+struct PeerMaps {
+  CUtensorMap m[kMaxDst];
+};
+
+constexpr int kFlagReady = 0;
+constexpr int kFlagArrive = kMaxDst;
+static_assert(2 * kMaxDst == TLLM_SWIGLU_PEER_FLAG_WORDS, "flag words per rank");
+// About two seconds at the boost clock: far longer than any peer's launch skew in a healthy
+// job, short enough that a rank that never launches is reported instead of hanging.
+constexpr long long kPeerWaitLimitCycles = 4000000000LL;
+
+// One thread of CTA 0 at kernel start: tells every peer that this rank's call has begun, so
+// every earlier operation on this rank's stream (reads of its previous output included) is
+// complete and the peer may store into this rank's buffers.
+__device__ __forceinline__ void peer_signal(const Geom &g, int which) {
+  for (int d = 0; d < g.ndst; ++d)
+    if (d != g.rank) st_release_sys(g.flags[d] + which + g.rank, g.epoch);
+}
+
+// Waits until every peer has raised its word `which` of this rank's flags to this call's
+// epoch; gives up (records TLLM_DEV_WAIT_TIMEOUT + site, returns false) after the limit.
+__device__ __forceinline__ bool peer_wait(const Geom &g, int which, int site) {
+  const uint32_t *mine = g.flags[g.rank] + which;
+  const long long t0 = clock64();
+  for (int s = 0; s < g.ndst; ++s) {
+    if (s == g.rank) continue;
+    while (static_cast<int>(ld_acquire_sys(mine + s) - g.epoch) < 0) {
+      if (clock64() - t0 > kPeerWaitLimitCycles) {
+        atomicCAS(&g_swiglu_status, 0, TLLM_DEV_WAIT_TIMEOUT + site);
+        return false;
+      }
+      __nanosleep(128);
+    }
+  }
+  return true;
+}
+
+// One thread per CTA once every store of the CTA has completed: the last CTA of the launch
+// tells every peer that this rank's stores into it are complete, then waits until every peer
+// has said the same, so the launch ends only once this rank's [M, N_total] output is whole.
+__device__ __forceinline__ void peer_finish(const Geom &g, int site) {
+  __threadfence_system();
+  const uint32_t prev = atomicAdd(g.done, 1u);
+  if (prev != gridDim.x - 1) return;
+  __threadfence_system();
+  *g.done = 0u;  // the next launch on this stream starts after this one ends
+  peer_signal(g, kFlagArrive);
+  peer_wait(g, kFlagArrive, site);
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 
 template <typename T>
 __device__ __forceinline__ void store_row_chunk(T *orow, int n_base, int N, bool vec,
@@ -130,6 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                      const __grid_constant__ CUtensorMap tm_w1,
                      const __grid_constant__ CUtensorMap tm_w3, T *__restrict__ out,
                      const Geom g) {
+  const bool handshake = kPeers && g.flags[0] != nullptr;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -140,11 +211,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *tempty = bars + 2 * STAGES + 2;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+  volatile int *peer_ok = reinterpret_cast<volatile int *>(tmem_holder + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   constexpr bool kBF16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
 
+  if (handshake && blockIdx.x == 0 && threadIdx.x == 2 * 32) peer_signal(g, kFlagReady);
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(smem_u32(&full[s]), 1);
@@ -261,6 +334,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad = warp & 3;  // TMEM lanes this warp may access
     const int row = quad * 32 + lane;
     uint8_t *peer_stage = smem + SMEM_BYTES - 1024;  // past the barrier block (peer mode only)
+    // Peer mode: no store into a peer before the peer's call has begun (its earlier reads of
+    // the buffer are complete); the first tile's main loop runs meanwhile.
+    bool remote_ok = true;
+    if (handshake) {
+      if (threadIdx.x == 2 * 32) *peer_ok = peer_wait(g, kFlagReady, SITE_PEER_READY) ? 1 : 0;
+      named_bar_sync(1, kEpiThreads);
+      remote_ok = *peer_ok != 0;
+    }
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -307,6 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
 #pragma unroll 1
             for (int d = 0; d < g.ndst; ++d) {
+              if (d != g.rank && !remote_ok) continue;
               T *drow = static_cast<T *>(g.dst[d]) + static_cast<int64_t>(m) * g.ldo + g.col_off;
               store_row_chunk<T>(drow, n0 + c, g.N, false, v);
             }
@@ -320,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t off = static_cast<int64_t>(m) * g.ldo + g.col_off + n0;
 #pragma unroll 1
         for (int d = 0; d < g.ndst; ++d)
-          bulk_store(static_cast<T *>(g.dst[d]) + off, src, staged * 64);
+          if (d == g.rank || remote_ok) bulk_store(static_cast<T *>(g.dst[d]) + off, src, staged * 64);
         bulk_commit();
       }
       tc_fence_before();
@@ -330,7 +412,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc_phase ^= 1;
       }
     }
-    if (kPeers) bulk_wait_all();
+    if (kPeers) {
+      // This thread's copies have landed; order them (and its direct stores) before the
+      // system-scope completion signal.
+      bulk_wait_all();
+      fence_proxy_async_global();
+      __threadfence_system();
+    }
   }
 
   tc_fence_before();
@@ -339,6 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
+  if (handshake && threadIdx.x == 0) peer_finish(g, SITE_PEER_ARRIVE);
 }
 
 // =======================================================================================
@@ -356,16 +445,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   the leader's tempty barrier. TMEM is allocated and freed by one warp in each CTA with
 //   cta_group::2, between cluster barriers.
 // =======================================================================================
-constexpr int kPairStages = 6;
 constexpr int kPairStageBytes = A_BYTES + 2 * B_CHUNK_BYTES;  // 32 KB: x rows + one weight tile
-constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + 1024 + 1024;
+// Column-sharded mode: each epilogue warp stages its 32 rows x 128 columns of the finished
+// tile (two 64-column halves, 128-byte swizzled, 4 KB each) twice over, so the tensor stores
+// of one tile into every destination drain while the next tile is staged: 4 warps x 2 x 8 KB.
+constexpr int kPairPeerStageBytes = 4 * 2 * 8192;
+template <bool kPeers>
+struct PairCfg {
+  static constexpr int kStages = kPeers ? 5 : 6;  // the staging takes one stage's worth and more
+  static constexpr int kSmemBytes =
+      kStages * kPairStageBytes + 1024 + (kPeers ? kPairPeerStageBytes : 0) + 1024;
+};
+static_assert(PairCfg<true>::kSmemBytes <= 232448, "peer-mode pair kernel exceeds shared memory");
 
-template <typename T>
+template <typename T, bool kPeers>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     swiglu_pair_kernel(const __grid_constant__ CUtensorMap tm_x,
                        const __grid_constant__ CUtensorMap tm_w1,
                        const __grid_constant__ CUtensorMap tm_w3, T *__restrict__ out,
-                       const Geom g) {
+                       const Geom g, const __grid_constant__ PeerMaps pm) {
+  constexpr int kPairStages = PairCfg<kPeers>::kStages;
+  const bool handshake = kPeers && g.flags[0] != nullptr;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -376,6 +476,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t *tempty = bars + 2 * kPairStages + 2;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * kPairStages + 4);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+  volatile int *peer_ok = reinterpret_cast<volatile int *>(tmem_holder + 2);
+  // Peer mode: staging past the 1 KB barrier block (1024-byte aligned).
+  uint8_t *peer_stage = smem + kPairStages * kPairStageBytes + 1024;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -385,6 +488,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   constexpr bool kBF16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
   constexpr int kEpiWarps = kEpiThreads / 32;
 
+  if (handshake && blockIdx.x == 0 && threadIdx.x == 2 * 32) peer_signal(g, kFlagReady);
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPairStages; ++s) {
       mbar_init(smem_u32(&full[s]), 1);
@@ -505,9 +609,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int row = quad * 32 + lane;
     const uint32_t tempty_leader[2] = {mapa_shared(smem_u32(&tempty[0]), 0),
                                        mapa_shared(smem_u32(&tempty[1]), 0)};
+    bool remote_ok = true;
+    if (handshake) {
+      // No store into a peer before the peer's call has begun; the first main loop runs meanwhile.
+      if (threadIdx.x == 2 * 32) *peer_ok = peer_wait(g, kFlagReady, SITE_PEER_READY) ? 1 : 0;
+      named_bar_sync(1, kEpiThreads);
+      remote_ok = *peer_ok != 0;
+    }
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = pair; tile < num_tiles; tile += n_pairs) {
+    int it = 0;  // tiles this CTA has finished (peer mode: picks the staging buffer)
+    for (int tile = pair; tile < num_tiles; tile += n_pairs, ++it) {
       if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag,
                                              &g_swiglu_status, TLLM_DEV_WAIT_TIMEOUT + SITE_TFULL)))
         break;
@@ -517,6 +629,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * ACC_COLS;
       const int m = m0 + row;
       T *orow = out + static_cast<int64_t>(m) * g.ldo;
+      // Peer mode: this warp's staging buffer for this tile; the tensor stores that read it
+      // two tiles ago must have finished reading (the last tile's may still be in flight).
+      uint8_t *wst = peer_stage + quad * 16384 + (it & 1) * 8192;
+      if (kPeers) {
+        if (lane == 0 && it >= 2) bulk_wait_read<1>();
+        __syncwarp();
+      }
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t gr[32], ur[32];
@@ -529,15 +648,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const float uv = __uint_as_float(ur[j]);
           v[j] = (gv / (1.0f + expf(-gv))) * uv;
         }
-        if (m < g.M) store_row_chunk<T>(orow, n0 + c, g.N, g.vec_store != 0, v);
+        if (!kPeers) {
+          if (m < g.M) store_row_chunk<T>(orow, n0 + c, g.N, g.vec_store != 0, v);
+        } else {
+          // Row `lane` of the 64-column half c / 64, 16-byte units (c % 64) / 8 .. +3, placed
+          // by the 128-byte swizzle (unit ^ row % 8) the tensor maps expect.
+          uint8_t *hrow = wst + (c >> 6) * 4096 + lane * 128;
+          const int u0 = (c & 32) >> 3;
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            uint4 raw;
+            raw.x = Pack2<T>::pack(v[8 * jj + 0], v[8 * jj + 1]);
+            raw.y = Pack2<T>::pack(v[8 * jj + 2], v[8 * jj + 3]);
+            raw.z = Pack2<T>::pack(v[8 * jj + 4], v[8 * jj + 5]);
+            raw.w = Pack2<T>::pack(v[8 * jj + 6], v[8 * jj + 7]);
+            *reinterpret_cast<uint4 *>(hrow + (((u0 + jj) ^ (lane & 7)) << 4)) = raw;
+          }
+        }
       }
+      if (kPeers) fence_proxy_async_smem();  // staged rows visible to the tensor stores
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
+      if (kPeers && lane == 0) {
+        // The warp's 32 rows x 128 columns into every destination's slice; rows past M are
+        // clipped by the tensor maps.
+        const int y = m0 + quad * 32;
+#pragma unroll 1
+        for (int d = 0; d < g.ndst; ++d) {
+          if (d != g.rank && !remote_ok) continue;
+          tma_store_2d(&pm.m[d], smem_u32(wst), n0, y);
+          tma_store_2d(&pm.m[d], smem_u32(wst + 4096), n0 + 64, y);
+        }
+        bulk_commit();
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
       }
+    }
+    if (kPeers && lane == 0) {
+      bulk_wait_all();  // this warp's stores have landed in every destination
+      fence_proxy_async_global();
+      __threadfence_system();
     }
   }
 
@@ -548,6 +701,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
+  if (handshake && threadIdx.x == 0) peer_finish(g, SITE_PEER_ARRIVE);
 }
 
 // Layout-agnostic fallback (CUDA cores, fp32 accumulation) for shapes whose strides or
@@ -590,11 +744,24 @@ constexpr int kVariantAuto = 0;
 constexpr int kVariantSingleCta = 1;
 constexpr int kVariantCtaPair = 2;
 
+// Column-sharded destinations and the peer handshake (see Geom).
+struct PeerArgs {
+  void *const *dsts = nullptr;
+  int ndst = 0;
+  int64_t col_off = 0;
+  uint32_t *const *flags = nullptr;  // null: no handshake
+  int rank = 0;
+  uint32_t *done = nullptr;
+  uint32_t epoch = 0;
+};
+
 template <typename T>
 int launch(const void *x, const void *w1, const void *w3, void *out, int64_t M, int64_t N,
            int64_t K, int64_t lda, int64_t ldb1, int64_t ldb3, int64_t ldo, cudaStream_t st,
-           void *const *dsts = nullptr, int ndst = 0, int64_t col_off = 0,
-           int variant = kVariantAuto) {
+           const PeerArgs &pa = PeerArgs(), int variant = kVariantAuto) {
+  const int ndst = pa.ndst;
+  void *const *dsts = pa.dsts;
+  const int64_t col_off = pa.col_off;
   const bool tma_ok = lda % 8 == 0 && ldb1 % 8 == 0 && ldb3 % 8 == 0 && aligned16(x) &&
                       aligned16(w1) && aligned16(w3) && K % 8 == 0 && N % 8 == 0;
   if (!tma_ok && ndst > 0)
@@ -659,30 +826,49 @@ int launch(const void *x, const void *w1, const void *w3, void *out, int64_t M, 
   for (int d = 0; d < kMaxDst; ++d) {
     g.dst[d] = d < ndst ? dsts[d] : nullptr;
     if (d < ndst) dst_aligned = dst_aligned && aligned16(dsts[d]);
+    g.flags[d] = (pa.flags && d < ndst) ? pa.flags[d] : nullptr;
   }
+  g.rank = pa.rank;
+  g.done = pa.done;
+  g.epoch = pa.epoch;
   g.vec_store = (ldo % 8 == 0 && col_off % 8 == 0 && dst_aligned &&
                  (ndst > 0 || aligned16(out))) ? 1 : 0;
   const int sms = sm_count();
-  // The CTA pair needs the one-box weight tiles and pays off from two 128-row blocks up.
-  const bool pair_ok = ndst == 0 && w3d && sms >= 2;
+  // The CTA pair needs the one-box weight tiles and pays off from two 128-row blocks up. In
+  // the column-sharded mode it writes each destination through a tensor map of its slice.
+  const bool peer_maps_ok = ldo % 8 == 0 && col_off % 8 == 0 && dst_aligned;
+  const bool pair_ok = w3d && sms >= 2 && (ndst == 0 || peer_maps_ok);
   if (variant == kVariantCtaPair && !pair_ok)
-    return fail(TLLM_ERR_INVALID, "swiglu: the CTA-pair kernel needs N %% 128 == 0 and a local output");
+    return fail(TLLM_ERR_INVALID,
+                "swiglu: the CTA-pair kernel needs N %% 128 == 0 (and, column-sharded, 16-byte "
+                "aligned destinations, column offset and row stride)");
   if (pair_ok && (variant == kVariantCtaPair || (variant == kVariantAuto && M >= 2 * BM))) {
     Geom gp = g;
     gp.tiles_m = static_cast<int>((M + 2 * BM - 1) / (2 * BM));
     const int pair_tiles = gp.tiles_m * gp.tiles_n;
-    auto kern = swiglu_pair_kernel<T>;
+    PeerMaps pm;
+    memset(&pm, 0, sizeof(pm));
+    for (int d = 0; d < ndst; ++d) {
+      const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
+      const uint64_t strides[1] = {static_cast<uint64_t>(ldo) * 2};
+      const uint32_t box[2] = {64, 32};
+      const int rc = encode_tiled(&pm.m[d], dt, 2, static_cast<T *>(dsts[d]) + col_off, dims,
+                                  strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+    }
+    auto kern = ndst == 0 ? swiglu_pair_kernel<T, false> : swiglu_pair_kernel<T, true>;
+    const int smem = ndst == 0 ? PairCfg<false>::kSmemBytes : PairCfg<true>::kSmemBytes;
     // Persistent grid: as many pairs as can be resident at once (clusters are placed on SM
     // pairs of one GPC).
     KernelLaunchInfo info;
-    const int rc = prepare_kernel(reinterpret_cast<const void *>(kern), kPairSmemBytes, kThreads, 2, &info);
+    const int rc = prepare_kernel(reinterpret_cast<const void *>(kern), smem, kThreads, 2, &info);
     if (rc) return rc;
     const int max_clusters = info.resident;
     if (max_clusters < 1) return fail(TLLM_ERR_CUDA, "swiglu: the CTA-pair kernel cannot be resident");
     const int max_pairs = max_clusters < sms / 2 ? max_clusters : sms / 2;
     const int pairs = pair_tiles < max_pairs ? pair_tiles : max_pairs;
-    kern<<<2 * pairs, kThreads, kPairSmemBytes, st>>>(mx, m1, m3, static_cast<T *>(out), gp);
-    return cuda_status(cudaGetLastError(), "swiglu pair launch");
+    kern<<<2 * pairs, kThreads, smem, st>>>(mx, m1, m3, static_cast<T *>(out), gp, pm);
+    return cuda_status(cudaGetLastError(), ndst == 0 ? "swiglu pair launch" : "swiglu pair peers launch");
   }
   const int num_tiles = g.tiles_m * g.tiles_n;
   const int grid = num_tiles < sms ? num_tiles : sms;
@@ -747,11 +933,11 @@ extern "C" int tllm_swiglu_variant(const void *x, const void *w1, const void *w3
   TLLM_CHECK_ARG(x && w1 && w3 && out, "swiglu: null tensor pointer");
   TLLM_CHECK_ARG(lda >= K && ldb1 >= N && ldb3 >= N && ldo >= N, "swiglu: leading dimension too small");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const swiglu::PeerArgs none;
   if (dtype == TLLM_DTYPE_F16)
-    return swiglu::launch<__half>(x, w1, w3, out, M, N, K, lda, ldb1, ldb3, ldo, st, nullptr, 0, 0,
-                                  variant);
-  return swiglu::launch<__nv_bfloat16>(x, w1, w3, out, M, N, K, lda, ldb1, ldb3, ldo, st, nullptr, 0,
-                                       0, variant);
+    return swiglu::launch<__half>(x, w1, w3, out, M, N, K, lda, ldb1, ldb3, ldo, st, none, variant);
+  return swiglu::launch<__nv_bfloat16>(x, w1, w3, out, M, N, K, lda, ldb1, ldb3, ldo, st, none,
+                                       variant);
 }
 
 extern "C" int tllm_swiglu_colshard(const void *x, const void *w1, const void *w3,
@@ -774,9 +960,57 @@ extern "C" int tllm_swiglu_colshard(const void *x, const void *w1, const void *w
   TLLM_CHECK_ARG(K > 0 && x && w1 && w3, "swiglu column-sharded: K must be positive");
   TLLM_CHECK_ARG(lda >= K && ldb1 >= N && ldb3 >= N, "swiglu column-sharded: leading dimension too small");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  swiglu::PeerArgs pa;
+  pa.dsts = dsts;
+  pa.ndst = ndst;
+  pa.col_off = col_off;
   if (dtype == TLLM_DTYPE_F16)
-    return swiglu::launch<__half>(x, w1, w3, dsts[0], M, N, K, lda, ldb1, ldb3, ldo, st, dsts,
-                                  ndst, col_off);
-  return swiglu::launch<__nv_bfloat16>(x, w1, w3, dsts[0], M, N, K, lda, ldb1, ldb3, ldo, st,
-                                       dsts, ndst, col_off);
+    return swiglu::launch<__half>(x, w1, w3, dsts[0], M, N, K, lda, ldb1, ldb3, ldo, st, pa);
+  return swiglu::launch<__nv_bfloat16>(x, w1, w3, dsts[0], M, N, K, lda, ldb1, ldb3, ldo, st, pa);
+}
+
+extern "C" int tllm_swiglu_colshard_peers(const void *x, const void *w1, const void *w3,
+                                          void *const *dsts, uint32_t *const *flags, int ndst,
+                                          int rank, uint32_t *done, uint32_t epoch, int64_t M,
+                                          int64_t N, int64_t K, int64_t lda, int64_t ldb1,
+                                          int64_t ldb3, int64_t ldo, int dtype, int variant,
+                                          void *stream) {
+  using namespace tllm;
+  clear_error();
+  TLLM_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "swiglu column-sharded: negative dimension");
+  TLLM_CHECK_ARG(dtype == TLLM_DTYPE_F16 || dtype == TLLM_DTYPE_BF16,
+                 "swiglu column-sharded: unsupported dtype %d", dtype);
+  TLLM_CHECK_ARG(variant >= 0 && variant <= 2, "swiglu column-sharded: unknown kernel variant %d",
+                 variant);
+  TLLM_CHECK_ARG(dsts && flags && done && ndst >= 1 && ndst <= swiglu::kMaxDst,
+                 "swiglu column-sharded: 1..%d destinations, their flags and a done counter required",
+                 swiglu::kMaxDst);
+  TLLM_CHECK_ARG(rank >= 0 && rank < ndst, "swiglu column-sharded: rank %d outside 0..%d", rank,
+                 ndst - 1);
+  TLLM_CHECK_ARG(epoch != 0, "swiglu column-sharded: epoch 0 is the flags' initial value");
+  TLLM_CHECK_ARG(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31),
+                 "swiglu column-sharded: dimension too large");
+  const int64_t col_off = static_cast<int64_t>(rank) * N;
+  TLLM_CHECK_ARG(ldo >= static_cast<int64_t>(ndst) * N, "swiglu column-sharded: row stride below N * ranks");
+  for (int d = 0; d < ndst; ++d)
+    TLLM_CHECK_ARG(dsts[d] && flags[d], "swiglu column-sharded: null destination or flags %d", d);
+  // Every rank takes part in every call, empty or not: a call that returned early here would
+  // leave its peers waiting for this rank's flags.
+  TLLM_CHECK_ARG(M > 0 && N > 0 && K > 0 && x && w1 && w3,
+                 "swiglu column-sharded: M, N and K must be positive");
+  TLLM_CHECK_ARG(lda >= K && ldb1 >= N && ldb3 >= N, "swiglu column-sharded: leading dimension too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  swiglu::PeerArgs pa;
+  pa.dsts = dsts;
+  pa.ndst = ndst;
+  pa.col_off = col_off;
+  pa.flags = flags;
+  pa.rank = rank;
+  pa.done = done;
+  pa.epoch = epoch;
+  if (dtype == TLLM_DTYPE_F16)
+    return swiglu::launch<__half>(x, w1, w3, dsts[rank], M, N, K, lda, ldb1, ldb3, ldo, st, pa,
+                                  variant);
+  return swiglu::launch<__nv_bfloat16>(x, w1, w3, dsts[rank], M, N, K, lda, ldb1, ldb3, ldo, st, pa,
+                                       variant);
 }

@@ -11,9 +11,10 @@ The reference is single-GPU only. Across the GPUs of one node the operators shar
 * swiglu over output columns: rank r holds x and the column slices w1[:, Nr], w3[:, Nr] and
   computes out[:, Nr] (``swiglu_column_sharded``). With ``PeerBuffers`` (the default in the
   benchmark) the GEMM epilogue stores each output tile straight into every rank's [M, N]
-  buffer over NVLink, so there is no separate all-gather pass; without them the slices are
-  all-gathered with NCCL and permuted into [M, N] (row chunks let the gather of chunk c
-  overlap the GEMM of chunk c+1).
+  buffer over NVLink, so there is no separate all-gather pass, and the kernel synchronises
+  with its peers itself through flag words in every rank's memory (no host barrier, no NCCL
+  call per step); without them the slices are all-gathered with NCCL and permuted into
+  [M, N] (row chunks let the gather of chunk c overlap the GEMM of chunk c+1).
 
 The per-rank compute function is a parameter only so the partitioning and gather logic can
 be exercised on CPU ranks (gloo); the default is the CUDA operator.
@@ -109,51 +110,92 @@ def column_range(n: int, rank: int, world: int, align: int = 8) -> tuple[int, in
     return rank * per, (rank + 1) * per
 
 
+# IPC mappings opened by this process: allocation handle -> [base pointer, users]. Small
+# tensors of one rank can share an allocation (the caching allocator sub-allocates), so a
+# handle is opened once and closed when its last user is done.
+_IPC_OPEN: dict[bytes, list] = {}
+
+
+def _ipc_open(handle: bytes, offset: int) -> tuple[int, bytes]:
+    from tritonllmcompiler_b200 import _lib
+
+    ent = _IPC_OPEN.get(handle)
+    if ent is None:
+        ptr, base = ctypes.c_void_p(), ctypes.c_void_p()
+        _lib.check(_lib.load().tllm_ipc_open(handle, 0, ctypes.byref(ptr), ctypes.byref(base)))
+        ent = _IPC_OPEN[handle] = [base.value, 0]
+    ent[1] += 1
+    return ent[0] + offset, handle
+
+
+def _ipc_release(handle: bytes) -> None:
+    from tritonllmcompiler_b200 import _lib
+
+    ent = _IPC_OPEN.get(handle)
+    if ent is None:
+        return
+    ent[1] -= 1
+    if ent[1] == 0:
+        del _IPC_OPEN[handle]
+        _lib.load().tllm_ipc_close(ent[0])
+
+
 class PeerBuffers:
     """[rows, cols] output buffers on every rank, each mapped into every rank's process
-    (CUDA IPC), used in ``slots`` alternating copies.
+    (CUDA IPC), used in ``slots`` alternating copies, plus the flag words through which the
+    column-sharded kernel synchronises with its peers.
 
     ``ptrs[slot][r]`` is rank r's buffer of that slot as seen from this process;
-    ``locals[slot]`` is this rank's own tensor. With two slots a call's output stays valid
-    until the call after next, as long as whatever reads it is ordered on the same stream
-    before that call; with one slot each call also waits for every rank to be done with the
-    previous output. Create once per output shape (opening IPC handles is slow) and
+    ``locals[slot]`` is this rank's own tensor. A call stores into a peer only after the
+    peer's own call has begun, and ends only once every peer's stores into this rank have
+    landed, so a call's output is complete when its launch ends and stays valid until this
+    rank's next call with the same slot (the call after next with two slots). Every rank
+    must make every call. Create once per output shape (opening IPC handles is slow) and
     ``close()`` before the process group goes away.
     """
 
-    def __init__(self, shape, dtype, device, group=None, slots: int = 2):
-        from tritonllmcompiler_b200 import _lib
+    FLAG_WORDS = 16  # TLLM_SWIGLU_PEER_FLAG_WORDS
 
+    def __init__(self, shape, dtype, device, group=None, slots: int = 2):
         assert slots in (1, 2)
-        lib = _lib.load()
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        assert self.world <= 8, "the column-sharded kernel writes at most 8 destinations"
         self.slots = slots
         self.calls = 0
-        self.locals = [torch.empty(shape, dtype=dtype, device=device) for _ in range(slots)]
-        self.ptrs: list[list[int]] = []
-        self._bases: list[int] = []
-        for t in self.locals:
-            handle = (ctypes.c_char * 64)()
-            offset = ctypes.c_uint64(0)
-            with torch.cuda.device(device):
-                _lib.check(lib.tllm_ipc_get_handle(t.data_ptr(), handle, ctypes.byref(offset)))
-            infos = [None] * self.world
-            dist.all_gather_object(infos, (bytes(handle), offset.value), group=group)
-            ptrs = []
-            with torch.cuda.device(device):
-                for r, (hb, off) in enumerate(infos):
-                    if r == self.rank:
-                        ptrs.append(t.data_ptr())
-                        continue
-                    ptr, base = ctypes.c_void_p(), ctypes.c_void_p()
-                    _lib.check(lib.tllm_ipc_open(hb, off, ctypes.byref(ptr), ctypes.byref(base)))
-                    ptrs.append(ptr.value)
-                    self._bases.append(base.value)
-            self.ptrs.append(ptrs)
+        self.device = torch.device(device)
+        self._handles: list[bytes] = []
+        with torch.cuda.device(self.device):
+            self.locals = [torch.empty(shape, dtype=dtype, device=self.device) for _ in range(slots)]
+            self.flags = torch.zeros(self.FLAG_WORDS, dtype=torch.int32, device=self.device)
+            self.done = torch.zeros(1, dtype=torch.int32, device=self.device)
+            torch.cuda.synchronize()  # zeroed before any peer can write a flag
+        self.ptrs: list[list[int]] = [self._share(t) for t in self.locals]
         self._arrs = [(ctypes.c_void_p * self.world)(*p) for p in self.ptrs]
-        self._flag = torch.zeros(1, dtype=torch.float32, device=device)
+        self._flag_arr = (ctypes.c_void_p * self.world)(*self._share(self.flags))
+
+    def _share(self, t: torch.Tensor) -> list[int]:
+        """Every rank's tensor `t` (same role) as a pointer in this process."""
+        from tritonllmcompiler_b200 import _lib
+
+        lib = _lib.load()
+        handle = (ctypes.c_char * 64)()
+        offset = ctypes.c_uint64(0)
+        with torch.cuda.device(self.device):
+            _lib.check(lib.tllm_ipc_get_handle(t.data_ptr(), handle, ctypes.byref(offset)))
+        infos = [None] * self.world
+        dist.all_gather_object(infos, (bytes(handle), offset.value), group=self.group)
+        ptrs = []
+        with torch.cuda.device(self.device):
+            for r, (hb, off) in enumerate(infos):
+                if r == self.rank:
+                    ptrs.append(t.data_ptr())
+                    continue
+                p, h = _ipc_open(hb, off)
+                ptrs.append(p)
+                self._handles.append(h)
+        return ptrs
 
     @property
     def local(self) -> torch.Tensor:
@@ -161,16 +203,13 @@ class PeerBuffers:
         return self.locals[self.calls % self.slots]
 
     def close(self):
-        from tritonllmcompiler_b200 import _lib
-
-        lib = _lib.load()
-        with torch.cuda.device(self.locals[0].device):
-            for b in self._bases:
-                lib.tllm_ipc_close(b)
-        self._bases = []
+        with torch.cuda.device(self.device):
+            for h in self._handles:
+                _ipc_release(h)
+        self._handles = []
 
 
-def _swiglu_into_peers(x, w1_local, w3_local, peers: PeerBuffers, group):
+def _swiglu_into_peers(x, w1_local, w3_local, peers: PeerBuffers, variant: int = 0):
     from tritonllmcompiler_b200 import _lib
 
     m, k = x.shape
@@ -179,16 +218,13 @@ def _swiglu_into_peers(x, w1_local, w3_local, peers: PeerBuffers, group):
     out = peers.locals[slot]
     assert out.shape == (m, n_loc * peers.world) and out.dtype == x.dtype
     assert x.stride(1) == 1 and w1_local.stride(1) == 1 and w3_local.stride(1) == 1
-    if peers.slots == 1:
-        # Every rank has finished with its previous output before any peer writes into it.
-        dist.all_reduce(peers._flag, group=group)
+    epoch = peers.calls % 0xFFFFFFFF + 1  # 1 .. 2^32 - 1, then 1 again; never 0 (the initial flags)
     with torch.cuda.device(x.device):
-        _lib.check(_lib.load().tllm_swiglu_colshard(
-            x.data_ptr(), w1_local.data_ptr(), w3_local.data_ptr(), peers._arrs[slot], peers.world,
-            peers.rank * n_loc, m, n_loc, k, x.stride(0), w1_local.stride(0), w3_local.stride(0),
-            out.stride(0), _lib.DTYPE_CODES[x.dtype], _lib.stream_of(x)))
-    # Every peer's tiles have landed in this rank's buffer.
-    dist.all_reduce(peers._flag, group=group)
+        _lib.check(_lib.load().tllm_swiglu_colshard_peers(
+            x.data_ptr(), w1_local.data_ptr(), w3_local.data_ptr(), peers._arrs[slot],
+            peers._flag_arr, peers.world, peers.rank, peers.done.data_ptr(), epoch, m, n_loc, k,
+            x.stride(0), w1_local.stride(0), w3_local.stride(0), out.stride(0),
+            _lib.DTYPE_CODES[x.dtype], variant, _lib.stream_of(x)))
     peers.calls += 1
     return out
 
@@ -196,17 +232,19 @@ def _swiglu_into_peers(x, w1_local, w3_local, peers: PeerBuffers, group):
 def swiglu_column_sharded(x: torch.Tensor, w1_local: torch.Tensor, w3_local: torch.Tensor,
                           group=None, *, chunks: int = 1, op: Callable | None = None,
                           out: torch.Tensor | None = None,
-                          peers: PeerBuffers | None = None) -> torch.Tensor:
+                          peers: PeerBuffers | None = None, variant: int = 0) -> torch.Tensor:
     """out = silu(x @ w1) * (x @ w3) with w1/w3 column-sharded over the process group.
 
     Every rank passes the full x [M, K] and its column slices [K, N/g]; every rank returns
     the full [M, N] output. With ``peers`` (CUDA, one node) the kernel writes every rank's
-    output directly and this rank's buffer of the slot just written is returned. Otherwise the slices are all-gathered;
+    output directly and this rank's buffer of the slot just written is returned (``variant``
+    picks the kernel: 0 automatic, 1 one CTA per tile, 2 CTA pairs). Otherwise the slices are
+    all-gathered;
     with chunks > 1 the rows are processed in `chunks` blocks and the all-gather of block c
     runs on a side stream (CUDA) while block c+1 computes.
     """
     if peers is not None:
-        return _swiglu_into_peers(x, w1_local, w3_local, peers, group)
+        return _swiglu_into_peers(x, w1_local, w3_local, peers, variant)
     if op is None:
         from tritonllmcompiler_b200.ops.swiglu import swiglu as op
     world = dist.get_world_size(group)
