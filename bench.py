@@ -306,14 +306,18 @@ def cpu_flash_baseline(b, h, s, d, causal, heads, threads=None):
     from oracle import ops_oracle as O
 
     threads = threads or cpu_cores()
+    heads = max(heads, min(threads, b * h))
     rng = np.random.default_rng(2)
     qkv = [tuple(_normal_f16(rng, (1, 1, s, d)) for _ in range(3)) for _ in range(heads)]
-    el = _parallel(qkv, lambda t: O.flash_attention(*t, causal=causal), min(threads, heads))
+    el, reps = 0.0, 0
+    while el < 2.0 and reps < 20:
+        el += _parallel(qkv, lambda t: O.flash_attention(*t, causal=causal), min(threads, heads))
+        reps += 1
     flops_head = 4.0 * s * s * d * (0.5 if causal else 1.0)
-    return {"value": flops_head * heads / el / 1e12, "unit": "TFLOP/s", "cores": min(threads, heads),
-            "kind": "port",
-            "sample": f"{heads} of {b * h} heads [S={s}, D={d}{', causal' if causal else ''}] in "
-                      f"{el:.1f} s, one head per thread; extrapolated to the full problem"}
+    return {"value": flops_head * heads * reps / el / 1e12, "unit": "TFLOP/s",
+            "cores": min(threads, heads), "kind": "port",
+            "sample": f"{reps} x {heads} of {b * h} heads [S={s}, D={d}{', causal' if causal else ''}] "
+                      f"in {el:.1f} s, one head per thread; extrapolated to the full problem"}
 
 
 def cpu_paged_baseline(lens, h, d, bs, threads=None):
@@ -335,11 +339,14 @@ def cpu_paged_baseline(lens, h, d, bs, threads=None):
         bt = np.arange(nb, dtype=np.int32)[None]
         cases.append((q, kc, vc, bt, np.array([n], np.int32)))
         nbytes += n * h * d * 2 * 2 + 2 * h * d * 2 + nb * 4 + 4
-    el = _parallel(cases, lambda c: O.paged_attention(*c, block_size=bs), min(threads, len(lens)))
-    return {"value": nbytes / el / 1e9, "unit": "GB/s", "cores": min(threads, len(lens)),
+    el, reps = 0.0, 0
+    while el < 2.0 and reps < 20:
+        el += _parallel(cases, lambda c: O.paged_attention(*c, block_size=bs), min(threads, len(lens)))
+        reps += 1
+    return {"value": nbytes * reps / el / 1e9, "unit": "GB/s", "cores": min(threads, len(lens)),
             "kind": "port",
-            "sample": f"{len(lens)} sequences (lengths {min(lens)}..{max(lens)}, H={h}, D={d}, "
-                      f"block {bs}) in {el:.1f} s, one sequence per thread; extrapolated"}
+            "sample": f"{reps} x {len(lens)} sequences (lengths {min(lens)}..{max(lens)}, H={h}, "
+                      f"D={d}, block {bs}) in {el:.1f} s, one sequence per thread; extrapolated"}
 
 
 # Single-operator cases (used to profile one kernel at a time from committed code).
@@ -673,6 +680,17 @@ def extra_ops(torch, T, peaks, peak_src, with_cpu=True):
                "roofline": _roofline(gbs, hbm, "GB/s", "hbm", hbm_src, traffic,
                                      "rmsnorm_rope_vec_kernel")}
         if cfg:
+            # 557 KB is below launch latency: the same operator on one row, timed the same way,
+            # gives the floor of a single timed launch; 100 calls between one pair of events
+            # give the per-call cost once launches overlap.
+            x1 = x[:1, :1, :1].contiguous()
+            ent["one_row_launch_ms"] = _median_ms(torch, lambda: T.rmsnorm_rope(x1, w, cos, sin), 20, 5, flush)
+
+            def hundred():
+                for _ in range(100):
+                    T.rmsnorm_rope(x, w, cos, sin)
+
+            ent["per_call_ms_100_back_to_back"] = _median_ms(torch, hundred, 5, 2, flush) / 100
             hx, hw, hc, hs = (_pinned_like(torch, t_) for t_ in (x, w, cos, sin))
             hout = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
             dx, dw, dc, ds = (torch.empty_like(t_) for t_ in (x, w, cos, sin))
@@ -738,7 +756,7 @@ def extra_ops(torch, T, peaks, peak_src, with_cpu=True):
     ent["e2e"] = e
     if with_cpu:
         lens64, _ = _paged_meta(64)
-        ent["cpu_baseline"] = cpu_paged_baseline(lens64[:8], 32, 128, 16)
+        ent["cpu_baseline"] = cpu_paged_baseline(lens64[:16], 32, 128, 16)
     res["paged_decode_b64_h32_d128_bs16"] = ent
     del kc, vc, hk, hv
     torch.cuda.empty_cache()
@@ -896,7 +914,8 @@ def _timed_ranks(torch, dist, world, fn, steps, warmup, flush=None):
 def sharded_cfg5(torch, dist, T, S, world, rank, local, peaks, peak_src, with_cpu):
     """The Llama-3-70B-shaped sharded workloads at this world size (every rank)."""
     res = {}
-    tc = peaks["bf16_tflops"]
+    # These kernels run for milliseconds back to back: the sustained (power-capped) peak.
+    tc = peaks["bf16_tflops_sustained"]
     hbm = peaks["hbm_gbs"]
     dev = torch.device("cuda", local)
 
@@ -935,7 +954,7 @@ def sharded_cfg5(torch, dist, T, S, world, rank, local, peaks, peak_src, with_cp
            "roofline": {"bound": "tensor" if t_tc >= t_link else "nvlink",
                         "target_ms": max(t_tc, t_link) * 1e3, "tensor_ms": t_tc * 1e3,
                         "nvlink_ms": t_link * 1e3, "frac": max(t_tc, t_link) * 1e3 / ms,
-                        "note": f"slower of local FLOPs / {peak_src} bf16 peak {tc:.0f} TFLOP/s and "
+                        "note": f"slower of local FLOPs / {peak_src} sustained bf16 peak {tc:.0f} TFLOP/s and "
                                 f"bytes sent per rank / {NVLINK_GBS:.0f} GB/s peer-copy rate"}}
     if world > 1:
         ent["nvlink_gbs_per_rank"] = (world - 1) * M * n_loc * 2 / (ms * 1e-3) / 1e9
@@ -971,7 +990,7 @@ def sharded_cfg5(torch, dist, T, S, world, rank, local, peaks, peak_src, with_cp
     ent = {"value": tf, "unit": "TFLOP/s", "ms": ms, "flops": flops,
            "per_rank": f"heads [{h0}, {h1}) of q/k/v/o, no communication",
            "checksum_fp16_bits": chk,
-           "roofline": _roofline(tf / world, tc, "TFLOP/s", "tensor", f"{peak_src} bf16_tflops",
+           "roofline": _roofline(tf / world, tc, "TFLOP/s", "tensor", f"{peak_src} bf16_tflops_sustained",
                                  kernel="flash_pp_kernel", note="achieved per GPU")}
     if with_cpu:
         ent["cpu_baseline"] = cpu_flash_baseline(B, H, Sq, D, True, 4, threads=4)

@@ -165,6 +165,9 @@ TLLM_API int tllm_rmsnorm_rope(const void *x, const void *w, const void *cos, co
  * and the fp32 C-ABI cutlass_gemm_swiglu / cutlass_gemm_swiglu_sm90 of
  * mlir/runtime/cutlass_c_api.h:10-18. x [M,K] row stride lda, w1/w3 [K,N] row strides
  * ldb1/ldb3, out [M,N] row stride ldo (all elements; inner strides are 1).
+ * Performance limit: the tensor-core kernels need K, N, lda, ldb1 and ldb3 multiples of 8
+ * and x, w1, w3 16-byte aligned (what a TMA descriptor can describe); other shapes run on a
+ * CUDA-core kernel with the same results at roughly 1/50 of the speed.
  */
 TLLM_API int tllm_swiglu(const void *x, const void *w1, const void *w3, void *out, int64_t M,
                 int64_t N, int64_t K, int64_t lda, int64_t ldb1, int64_t ldb3,

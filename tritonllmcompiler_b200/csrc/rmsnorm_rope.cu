@@ -129,10 +129,11 @@ int launch(const void *x, const void *w, const void *c, const void *s, void *o, 
     // Heads per thread group: 8 (or 4, 2) when H allows it and there is work for every SM
     // many times over; two 256-thread blocks stay resident per SM (register cap 128).
     const int64_t H = g.H;
+    const int64_t sms = sm_count() > 0 ? sm_count() : 148;
     int R = 1;
-    if (H % 8 == 0 && rows >= 8LL * 148 * 256) R = 8;
-    else if (H % 4 == 0 && rows >= 4LL * 148 * 256) R = 4;
-    else if (H % 2 == 0 && rows >= 2LL * 148 * 256) R = 2;
+    if (H % 8 == 0 && rows >= 8LL * sms * 256) R = 8;
+    else if (H % 4 == 0 && rows >= 4LL * sms * 256) R = 4;
+    else if (H % 2 == 0 && rows >= 2LL * sms * 256) R = 2;
     const int64_t groups = rows / R;
     const int64_t threads = groups * (D / 16);
     const unsigned grid = static_cast<unsigned>((threads + 255) / 256);
