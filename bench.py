@@ -684,7 +684,8 @@ def extra_ops(torch, T, peaks, peak_src, with_cpu=True):
             # gives the floor of a single timed launch; 100 calls between one pair of events
             # give the per-call cost once launches overlap.
             x1 = x[:1, :1, :1].contiguous()
-            ent["one_row_launch_ms"] = _median_ms(torch, lambda: T.rmsnorm_rope(x1, w, cos, sin), 20, 5, flush)
+            c1, s1 = cos[:1].contiguous(), sin[:1].contiguous()
+            ent["one_row_launch_ms"] = _median_ms(torch, lambda: T.rmsnorm_rope(x1, w, c1, s1), 20, 5, flush)
 
             def hundred():
                 for _ in range(100):
