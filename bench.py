@@ -367,6 +367,8 @@ OP_CASES = {
     "swiglu_fp8": "swiglu_fp8 e4m3 M4096 K4096 N14336, fp16 out",
     "flash_fp8_causal": "flash_attention_fp8 e4m3 causal [4,32,4096,128], fp16 out",
     "qkv_norm_rope": "qkv_norm_rope M4096 K4096 Hq32 Hkv8 D128 fp16 (Llama-3-8B QKV)",
+    "swiglu_colshard8_local": "column-sharded swiglu kernel of one of 8 ranks (M4096 K4096 N/8=1792), "
+                              "its 8 destination slices all on this GPU (no peer handshake)",
 }
 
 
@@ -523,6 +525,23 @@ def run_op(args):
         o, lse = flash_attention_fwd_lse(q, k, v, causal=True)
         fn = lambda: flash_attention_backward(q, k, v, o, lse, do, causal=True)  # noqa: E731
         work, unit = 2.5 * 4.0 * 4 * 32 * 4096 * 4096 * 128 * 0.5, "TFLOP/s"
+    elif op == "swiglu_colshard8_local":
+        # The column-sharded CTA-pair kernel exactly as one rank of 8 runs it, with the 8
+        # destinations (this rank's and 7 peers' [M, N] outputs) all allocated on this GPU, so
+        # the kernel can be profiled alone; HBM stands in for NVLink.
+        import ctypes
+
+        from tritonllmcompiler_b200 import _lib
+        M, K, N = SWIGLU_SHAPE
+        g8, n_loc = 8, N // 8
+        x, w1, w3 = rn((M, K)), rn((K, n_loc), K ** -0.5), rn((K, n_loc), K ** -0.5)
+        dsts = [torch.empty((M, N), dtype=torch.float16, device="cuda") for _ in range(g8)]
+        arr = (ctypes.c_void_p * g8)(*[d.data_ptr() for d in dsts])
+        lib = _lib.load()
+        fn = lambda: _lib.check(lib.tllm_swiglu_colshard(  # noqa: E731
+            x.data_ptr(), w1.data_ptr(), w3.data_ptr(), arr, g8, 3 * n_loc, M, n_loc, K, K, n_loc,
+            n_loc, N, 0, torch.cuda.current_stream().cuda_stream))
+        work, unit = 4.0 * M * K * n_loc, "TFLOP/s"
     elif op == "kv_append_rope":
         from tritonllmcompiler_b200.ops.paged_kv import paged_kv_append_rope
         kn, vn, kc, vc, bt, start, w, cos, sin, work = _append_inputs(torch)
