@@ -1172,6 +1172,12 @@ def run_ours(args):
                              "bf16 peak and bytes sent per rank / NVLink rate")
         traffic = profile_traffic(f"swiglu_pair_kernel_peers_m4096_k4096_n14336_g{world}.md")
         roofline["traffic"] = traffic
+        # The one-CTA column-sharded kernel (128 x 128 tiles, half a CTA pair's tile time, so
+        # the first stores leave earlier) on the same step, for comparison.
+        ms1 = _max_over_ranks(torch, dist, world, _median_ms(
+            torch, lambda: S.swiglu_column_sharded(x, w1l, w3l, peers=peers, variant=1),
+            max(5, args.steps // 2), 2, flush))
+        roofline["one_cta_kernel_ms"] = ms1
 
     # End to end through the public API with pinned host buffers (H2D inputs, D2H result).
     hx = x.cpu().pin_memory()
