@@ -152,3 +152,38 @@ def test_localize_blocks_matches_global_view():
         local = O.paged_attention(q[part].float().numpy(), kc[ids].float().numpy(),
                                   vc[ids].float().numpy(), lbt.numpy(), lcl.numpy(), block_size=bs)
         assert np.array_equal(local, full[part])
+
+
+def test_ipc_handles_are_opened_once_and_closed_by_the_last_user(monkeypatch):
+    """Small tensors of one rank can share an allocation (the caching allocator sub-allocates),
+    so their IPC handles can be equal: the mapping is opened once and closed only when its last
+    user releases it. Checked with a stand-in for the library's IPC calls (no GPU)."""
+    import ctypes
+
+    from tritonllmcompiler_b200 import _lib
+
+    calls = []
+
+    class FakeLib:
+        def tllm_ipc_open(self, handle, offset, ptr, base):
+            calls.append(("open", handle))
+            ctypes.cast(base, ctypes.POINTER(ctypes.c_void_p))[0] = 0x10000
+            return 0
+
+        def tllm_ipc_close(self, base):
+            calls.append(("close", base))
+            return 0
+
+    monkeypatch.setattr(_lib, "load", lambda: FakeLib())
+    h1, h2 = b"A" * 64, b"B" * 64
+    p, h = S._ipc_open(h1, 256)
+    assert p == 0x10000 + 256 and h == h1
+    assert S._ipc_open(h1, 512)[0] == 0x10000 + 512  # same allocation: no second open
+    S._ipc_open(h2, 0)
+    assert [c[0] for c in calls] == ["open", "open"]
+    S._ipc_release(h1)
+    assert [c[0] for c in calls] == ["open", "open"]  # one user of h1 left
+    S._ipc_release(h1)
+    S._ipc_release(h2)
+    assert [c[0] for c in calls] == ["open", "open", "close", "close"]
+    assert not S._IPC_OPEN
