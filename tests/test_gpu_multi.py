@@ -3,7 +3,8 @@ operators on the same inputs. Skipped when fewer GPUs are visible than the case 
 
 Per world size, one group of processes runs every mode:
 * swiglu column-sharded, the all-gather fused into the GEMM epilogue with the in-kernel peer
-  handshake: automatic kernel, forced one-CTA and CTA-pair kernels, one and two output slots,
+  handshake: automatic kernel, forced one-CTA and CTA-pair kernels (128-byte and 256-byte row
+  stores), one and two output slots,
   a column slice that is not a multiple of 128 (one-CTA kernel), several calls in a row with
   the output poisoned in between -- bit-identical to ``swiglu`` on one GPU;
 * swiglu column-sharded with the NCCL all-gather (1 and 2 row chunks) -- bit-identical;
@@ -42,7 +43,7 @@ def _swiglu_modes(rank, world, T, S, dist):
         n0, n1 = S.column_range(n, rank, world)
         w1l, w3l = w1[:, n0:n1].contiguous(), w3[:, n0:n1].contiguous()
         full = T.swiglu(x, w1, w3)
-        variants = [0, 1, 2] if n_loc % 128 == 0 else [0, 1]
+        variants = [0, 1, 2, 3] if n_loc % 128 == 0 else [0, 1]
         for slots in (1, 2):
             for variant in variants:
                 peers = S.PeerBuffers((m, n), x.dtype, x.device, slots=slots)
