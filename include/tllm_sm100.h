@@ -74,8 +74,7 @@ TLLM_API int tllm_flash_attn_fwd(const void *q, const void *k, const void *v, vo
  * implementations against each other: variant 0 = two 128-row query tiles per CTA with
  * ping-pong softmax warpgroups and work stealing (the default), 1 = one query tile per CTA,
  * 2 = variant 0 with one work item per CTA, 3 = variant 0 with P passed to P V through shared
- * memory instead of tensor memory (K and V tiles in one ring), 4 = variant 0 with the softmax
- * holding half a row of scores in registers at a time (the same result bit for bit). */
+ * memory instead of tensor memory (K and V tiles in one ring). */
 TLLM_API int tllm_flash_attn_fwd_variant(const void *q, const void *k, const void *v, void *o,
                                 int64_t B, int64_t H, int64_t Sq, int64_t Sk, int64_t D,
                                 const int64_t *sq, const int64_t *sk, const int64_t *sv,

@@ -290,15 +290,14 @@ def test_paged_int64_metadata_and_strided_q(cuda_device):
 def test_flash_kernel_variants_agree(cuda_device, b, h, s, d, causal):
     """The two-tile kernel (work stealing, the default), the single-tile kernel, the two-tile
     kernel with one item per CTA and the two-tile kernel with P in shared memory agree; work
-    stealing changes only which CTA computes an item, P holds the same values in TMEM or in
-    shared memory, and the half-row softmax (variant 4) computes the same maxima and
-    exponentials in the same order, so variants 0, 2, 3 and 4 match bit for bit."""
+    stealing changes only which CTA computes an item, and P holds the same values in TMEM or in
+    shared memory, so variants 0, 2 and 3 match bit for bit."""
     from tritonllmcompiler_b200 import _lib
 
     g = _gen(s + d)
     q, k, v = (torch.randn(b, h, s, d, generator=g).half().cuda() for _ in range(3))
     outs = []
-    for variant in (0, 1, 2, 3, 4):
+    for variant in (0, 1, 2, 3):
         o = torch.empty_like(q)
         _lib.check(_lib.load().tllm_flash_attn_fwd_variant(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), b, h, s, s, d,
@@ -309,5 +308,4 @@ def test_flash_kernel_variants_agree(cuda_device, b, h, s, d, causal):
         assert torch.allclose(outs[0].float(), o.float(), **G.tol(torch.float16))
     assert torch.equal(outs[0], outs[2])
     assert torch.equal(outs[0], outs[3])
-    assert torch.equal(outs[0], outs[4])
     assert _lib.debug_status() == 0

@@ -588,15 +588,13 @@ __device__ __forceinline__ uint32_t pack4_e4m3(float p0, float p1, float p2, flo
 // K-major, and P goes through shared memory as e4m3 (16 KB per query tile): the softmax frees
 // S_X as soon as it has loaded it, so QK_X(j+1) runs on the tensor core while P_X(j) is being
 // computed, instead of after PV_X(j).
-// kTP (P in TMEM only): the softmax holds half a row of scores in registers at a time.
-template <typename T, typename TI, int D, bool kSteal, bool kVarlen, bool kSP, bool kTP = false>
+template <typename T, typename TI, int D, bool kSteal, bool kVarlen, bool kSP>
 __global__ void __launch_bounds__(kPPThreads, 1)
     flash_pp_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const Args a) {
   constexpr bool kF8 = std::is_same<TI, __nv_fp8_e4m3>::value;
   static_assert(!kF8 || (!kVarlen && kSP), "e4m3 inputs: dense batches, P in shared memory");
-  static_assert(!kTP || !kSP, "half-row softmax: P in tensor memory");
   constexpr int EB = kF8 ? 1 : 2;
   using G = GeoPP<D, EB, kSP>;
   using PG = GeoPP<BN, EB>;  // a P tile has the layout of a Q tile with 128 columns
@@ -1042,58 +1040,29 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         tc_fence_after();
         const int k0 = j * BN;
         const bool need_mask = (k0 + BN > w.Sk) || (a.causal && k0 + BN - 1 > qx0);
-        // kTP: half a row (64 scores) in registers at a time, loaded from TMEM once for the
-        // row max and again for the exponentials.
-        auto load_half = [&](int hlf, uint32_t (&sh)[BN / 2]) {
-          tmem_ld2x32(s_tm + (BN / 2) * hlf, sh);
-          if (need_mask) {
+        // The whole S row in one TMEM round trip (four 32-column loads, one wait).
+        uint32_t sr[BN];
+        tmem_ld4x32(s_tm, sr);
+        if constexpr (kSP) {
+          // S_X(j) is in registers: QK_X(j+1) may overwrite it while P_X(j) is computed.
+          tc_fence_before();
+          mbar_arrive(smem_u32(&s_free[X]));
+        }
+        if (need_mask) {
 #pragma unroll
-            for (int t = 0; t < BN / 2; ++t) {
-              const int kg = k0 + (BN / 2) * hlf + t;
-              if (kg >= w.Sk || (a.causal && kg > qg)) sh[t] = __float_as_uint(-INFINITY);
-            }
+          for (int t = 0; t < BN; ++t) {
+            const int kg = k0 + t;
+            if (kg >= w.Sk || (a.causal && kg > qg)) sr[t] = __float_as_uint(-INFINITY);
           }
-        };
+        }
         // Row max on the raw scores (the scale is positive): an 8-way tree of 3-input maxima.
         float mx8[8];
-        // The whole S row in one TMEM round trip (four 32-column loads, one wait).
-        uint32_t sr[kTP ? 1 : BN];
-        if constexpr (kTP) {
 #pragma unroll
-          for (int hlf = 0; hlf < 2; ++hlf) {
-            uint32_t sh[BN / 2];
-            load_half(hlf, sh);
+        for (int t = 0; t < 8; ++t) mx8[t] = __uint_as_float(sr[t]);
 #pragma unroll
-            for (int t = 0; t < BN / 2; t += 2) {
-              if (hlf == 0 && t < 16) {
-                mx8[t >> 1] = fmaxf(__uint_as_float(sh[t]), __uint_as_float(sh[t + 1]));
-              } else {
-                mx8[(t >> 1) & 7] =
-                    max3f(mx8[(t >> 1) & 7], __uint_as_float(sh[t]), __uint_as_float(sh[t + 1]));
-              }
-            }
-          }
-        } else {
-          tmem_ld4x32(s_tm, sr);
-          if constexpr (kSP) {
-            // S_X(j) is in registers: QK_X(j+1) may overwrite it while P_X(j) is computed.
-            tc_fence_before();
-            mbar_arrive(smem_u32(&s_free[X]));
-          }
-          if (need_mask) {
-#pragma unroll
-            for (int t = 0; t < BN; ++t) {
-              const int kg = k0 + t;
-              if (kg >= w.Sk || (a.causal && kg > qg)) sr[t] = __float_as_uint(-INFINITY);
-            }
-          }
-#pragma unroll
-          for (int t = 0; t < 8; ++t) mx8[t] = __uint_as_float(sr[t]);
-#pragma unroll
-          for (int t = 8; t < BN; t += 2)
-            mx8[(t >> 1) & 7] =
-                max3f(mx8[(t >> 1) & 7], __uint_as_float(sr[t]), __uint_as_float(sr[t + 1]));
-        }
+        for (int t = 8; t < BN; t += 2)
+          mx8[(t >> 1) & 7] =
+              max3f(mx8[(t >> 1) & 7], __uint_as_float(sr[t]), __uint_as_float(sr[t + 1]));
         float mx = max3f(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], mx8[5]),
                          fmaxf(mx8[6], mx8[7]));
         mx *= a.scale_log2;
@@ -1168,16 +1137,10 @@ __global__ void __launch_bounds__(kPPThreads, 1)
 #pragma unroll
           for (int hlf = 0; hlf < 2; ++hlf) {
             uint32_t pk[32];
-            uint32_t sh[BN / 2];
-            if constexpr (kTP) {
-              load_half(hlf, sh);
-            } else {
-#pragma unroll
-              for (int t = 0; t < BN / 2; ++t) sh[t] = sr[kTP ? 0 : 64 * hlf + t];
-            }
 #pragma unroll
             for (int t = 0; t < 64; t += 2) {
-              const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sh[t]), __uint_as_float(sh[t + 1])),
+              const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sr[64 * hlf + t]),
+                                                 __uint_as_float(sr[64 * hlf + t + 1])),
                                          scale2, negm2);
               float x0, x1;
               f2_unpack(x2, x0, x1);
@@ -1281,7 +1244,6 @@ constexpr int kVariantPingPong = 0;
 constexpr int kVariantSingleTile = 1;
 constexpr int kVariantPingPongOneItem = 2;
 constexpr int kVariantSmemP = 3;  // P through shared memory, one K/V ring
-constexpr int kVariantHalfRow = 4;  // the softmax holds half a row of scores at a time
 
 // Packed variable-length batch: sequence b's rows are [cu_q[b], cu_q[b+1]) of q/o (total_q
 // rows) and [cu_k[b], cu_k[b+1]) of k/v (total_k rows, Hkv heads).
@@ -1395,8 +1357,7 @@ int launch_d(const void *q, const void *k, const void *v, void *o, int64_t B, in
   using GP = GeoPP<D>;
   auto kern = vl ? flash_pp_kernel<T, T, D, true, true, false>
                 : (variant == kVariantPingPongOneItem ? flash_pp_kernel<T, T, D, false, false, false>
-                   : (variant == kVariantHalfRow ? flash_pp_kernel<T, T, D, true, false, false, true>
-                                                 : flash_pp_kernel<T, T, D, true, false, false>));
+                                                      : flash_pp_kernel<T, T, D, true, false, false>);
   return launch_pp<GP>(kern, grid, mq, mk, mv, a, st);
 }
 
@@ -1488,8 +1449,7 @@ int entry(const void *q, const void *k, const void *v, void *o, int64_t B, int64
   TLLM_CHECK_ARG(dtype == TLLM_DTYPE_F16 || dtype == TLLM_DTYPE_BF16,
                  "flash_attention: unsupported dtype %d", dtype);
   TLLM_CHECK_ARG(variant == kVariantPingPong || variant == kVariantSingleTile ||
-                     variant == kVariantPingPongOneItem || variant == kVariantSmemP ||
-                     variant == kVariantHalfRow,
+                     variant == kVariantPingPongOneItem || variant == kVariantSmemP,
                  "flash_attention: unknown kernel variant %d", variant);
   TLLM_CHECK_ARG(sq && sk && sv && so, "flash_attention: null stride array");
   if (B == 0 || H == 0 || Sq == 0) return TLLM_OK;
