@@ -114,6 +114,13 @@ __device__ __forceinline__ void tma_store_2d(const void *map, uint32_t src, int 
                "r"(src), "r"(c0), "r"(c1)
                : "memory");
 }
+// Tensor store of one 3-D box from shared memory (tracked in the bulk async-group).
+__device__ __forceinline__ void tma_store_3d(const void *map, uint32_t src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
 __device__ __forceinline__ void tma_prefetch_desc(const void *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -97,6 +97,10 @@ struct Geom {
   int rank;
   uint32_t *done;
   uint32_t epoch;
+  // CTA-pair column-sharded kernel: the destination maps are 3-D {64 columns, N / 64, M} with
+  // boxes of {64, 2, 32}, so every row of a box leaves as one 256-byte span (instead of two
+  // 128-byte boxes per row block).
+  int store3d;
 };
 
 // Tensor maps of the destinations' column slices (column-sharded CTA-pair kernel): map d
@@ -400,9 +404,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async_smem();
         const uint32_t src = smem_u32(peer_stage + row * (BN * 2));
         const int64_t off = static_cast<int64_t>(m) * g.ldo + g.col_off + n0;
+        // Rotated destination order per row (see the CTA-pair kernel).
+        const int dstart = (static_cast<int>(blockIdx.x) + row) % g.ndst;
 #pragma unroll 1
-        for (int d = 0; d < g.ndst; ++d)
+        for (int i = 0; i < g.ndst; ++i) {
+          const int d = dstart + i < g.ndst ? dstart + i : dstart + i - g.ndst;
           if (d == g.rank || remote_ok) bulk_store(static_cast<T *>(g.dst[d]) + off, src, staged * 64);
+        }
         bulk_commit();
       }
       tc_fence_before();
@@ -653,7 +661,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         } else {
           // Row `lane` of the 64-column half c / 64, 16-byte units (c % 64) / 8 .. +3, placed
           // by the 128-byte swizzle (unit ^ row % 8) the tensor maps expect.
-          uint8_t *hrow = wst + (c >> 6) * 4096 + lane * 128;
+          // 3-D boxes: 128-byte row R = 2 * lane + c / 64 of the box, swizzled by R % 8.
+          const int srow = g.store3d ? 2 * lane + (c >> 6) : lane;
+          uint8_t *hrow = g.store3d ? wst + srow * 128 : wst + (c >> 6) * 4096 + lane * 128;
           const int u0 = (c & 32) >> 3;
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj) {
@@ -662,7 +672,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             raw.y = Pack2<T>::pack(v[8 * jj + 2], v[8 * jj + 3]);
             raw.z = Pack2<T>::pack(v[8 * jj + 4], v[8 * jj + 5]);
             raw.w = Pack2<T>::pack(v[8 * jj + 6], v[8 * jj + 7]);
-            *reinterpret_cast<uint4 *>(hrow + (((u0 + jj) ^ (lane & 7)) << 4)) = raw;
+            *reinterpret_cast<uint4 *>(hrow + (((u0 + jj) ^ (srow & 7)) << 4)) = raw;
           }
         }
       }
@@ -674,11 +684,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // The warp's 32 rows x 128 columns into every destination's slice; rows past M are
         // clipped by the tensor maps.
         const int y = m0 + quad * 32;
+        // Destinations in a rotated order (by CTA and warp), so that at any moment the SMs'
+        // stores spread over all peers instead of all targeting the same one.
+        const int dstart = (static_cast<int>(blockIdx.x) + quad) % g.ndst;
 #pragma unroll 1
-        for (int d = 0; d < g.ndst; ++d) {
+        for (int i = 0; i < g.ndst; ++i) {
+          const int d = dstart + i < g.ndst ? dstart + i : dstart + i - g.ndst;
           if (d != g.rank && !remote_ok) continue;
-          tma_store_2d(&pm.m[d], smem_u32(wst), n0, y);
-          tma_store_2d(&pm.m[d], smem_u32(wst + 4096), n0 + 64, y);
+          if (g.store3d) {
+            tma_store_3d(&pm.m[d], smem_u32(wst), 0, n0 >> 6, y);
+          } else {
+            tma_store_2d(&pm.m[d], smem_u32(wst), n0, y);
+            tma_store_2d(&pm.m[d], smem_u32(wst + 4096), n0 + 64, y);
+          }
         }
         bulk_commit();
       }
@@ -743,6 +761,7 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 constexpr int kVariantAuto = 0;
 constexpr int kVariantSingleCta = 1;
 constexpr int kVariantCtaPair = 2;
+constexpr int kVariantCtaPair3D = 3;  // column-sharded: CTA pairs storing 256-byte rows
 
 // Column-sharded destinations and the peer handshake (see Geom).
 struct PeerArgs {
@@ -831,6 +850,7 @@ int launch(const void *x, const void *w1, const void *w3, void *out, int64_t M, 
   g.rank = pa.rank;
   g.done = pa.done;
   g.epoch = pa.epoch;
+  g.store3d = 0;
   g.vec_store = (ldo % 8 == 0 && col_off % 8 == 0 && dst_aligned &&
                  (ndst > 0 || aligned16(out))) ? 1 : 0;
   const int sms = sm_count();
@@ -842,18 +862,31 @@ int launch(const void *x, const void *w1, const void *w3, void *out, int64_t M, 
     return fail(TLLM_ERR_INVALID,
                 "swiglu: the CTA-pair kernel needs N %% 128 == 0 (and, column-sharded, 16-byte "
                 "aligned destinations, column offset and row stride)");
-  if (pair_ok && (variant == kVariantCtaPair || (variant == kVariantAuto && M >= 2 * BM))) {
+  if (variant == kVariantCtaPair3D && !(pair_ok && ndst > 0))
+    return fail(TLLM_ERR_INVALID, "swiglu: variant 3 is the column-sharded CTA-pair kernel");
+  if (pair_ok && (variant == kVariantCtaPair || variant == kVariantCtaPair3D ||
+                  (variant == kVariantAuto && M >= 2 * BM))) {
     Geom gp = g;
     gp.tiles_m = static_cast<int>((M + 2 * BM - 1) / (2 * BM));
     const int pair_tiles = gp.tiles_m * gp.tiles_n;
     PeerMaps pm;
     memset(&pm, 0, sizeof(pm));
+    gp.store3d = variant == kVariantCtaPair3D ? 1 : 0;
     for (int d = 0; d < ndst; ++d) {
-      const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
-      const uint64_t strides[1] = {static_cast<uint64_t>(ldo) * 2};
-      const uint32_t box[2] = {64, 32};
-      const int rc = encode_tiled(&pm.m[d], dt, 2, static_cast<T *>(dsts[d]) + col_off, dims,
-                                  strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+      int rc;
+      if (gp.store3d) {
+        const uint64_t dims[3] = {64, static_cast<uint64_t>(N / 64), static_cast<uint64_t>(M)};
+        const uint64_t strides[2] = {128, static_cast<uint64_t>(ldo) * 2};
+        const uint32_t box[3] = {64, 2, 32};
+        rc = encode_tiled(&pm.m[d], dt, 3, static_cast<T *>(dsts[d]) + col_off, dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+      } else {
+        const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
+        const uint64_t strides[1] = {static_cast<uint64_t>(ldo) * 2};
+        const uint32_t box[2] = {64, 32};
+        rc = encode_tiled(&pm.m[d], dt, 2, static_cast<T *>(dsts[d]) + col_off, dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+      }
       if (rc) return rc;
     }
     auto kern = ndst == 0 ? swiglu_pair_kernel<T, false> : swiglu_pair_kernel<T, true>;
@@ -980,7 +1013,7 @@ extern "C" int tllm_swiglu_colshard_peers(const void *x, const void *w1, const v
   TLLM_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "swiglu column-sharded: negative dimension");
   TLLM_CHECK_ARG(dtype == TLLM_DTYPE_F16 || dtype == TLLM_DTYPE_BF16,
                  "swiglu column-sharded: unsupported dtype %d", dtype);
-  TLLM_CHECK_ARG(variant >= 0 && variant <= 2, "swiglu column-sharded: unknown kernel variant %d",
+  TLLM_CHECK_ARG(variant >= 0 && variant <= 3, "swiglu column-sharded: unknown kernel variant %d",
                  variant);
   TLLM_CHECK_ARG(dsts && flags && done && ndst >= 1 && ndst <= swiglu::kMaxDst,
                  "swiglu column-sharded: 1..%d destinations, their flags and a done counter required",
