@@ -1124,13 +1124,20 @@ def run_ours(args):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
+    # The clock sampler starts (NVML set-up, its thread) before the barrier, so that every rank
+    # enters the timed region together: at N > 1 a step waits inside the kernel for the ranks
+    # that start it late.
     with ClockSampler(local) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         times = _events_time(torch, step, args.steps, 0, flush)
     torch.cuda.synchronize()
     t_step = _max_over_ranks(torch, dist, world, sum(times) / len(times))
+    step_spread = {"median_ms": _max_over_ranks(torch, dist, world, statistics.median(times)),
+                   "max_ms": _max_over_ranks(torch, dist, world, max(times)),
+                   "min_ms": _max_over_ranks(torch, dist, world, min(times)),
+                   "note": "per-step CUDA-event times, each the max over ranks; ms_per_step is the mean"}
     if world > 1:
         dist.barrier()
     value = flops / (t_step * 1e-3) / 1e12
@@ -1243,6 +1250,7 @@ def run_ours(args):
         line = {
             "metric": "swiglu TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step,
+            "step_spread": step_spread,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic (seeded normal, x~N(0,1), w~N(0,1/K))",
             "config": headline_config(world, args.comm, args.chunks),
