@@ -1149,7 +1149,12 @@ __global__ void __launch_bounds__(kPPThreads, 1)
               ps2[(t >> 1) & 3] = f2_add(ps2[(t >> 1) & 3], f2_pack(p0, p1));
               pk[t >> 1] = Pack2<T>::pack(p0, p1);
             }
-            tmem_st32(s_tm + 32 * hlf, pk);
+            // The first half's store is not waited for on its own: the second half's store
+            // waits for both (+1 % in interleaved runs, the same output).
+            if (hlf == 0)
+              tmem_st32_nowait(s_tm, pk);
+            else
+              tmem_st32(s_tm + 32 * hlf, pk);
           }
         }
         float psa, psb, psc, psd, pse, psf, psg, psh;
