@@ -700,17 +700,10 @@ def extra_ops(torch, T, peaks, peak_src, with_cpu=True):
                                      "rmsnorm_rope_vec_kernel")}
         if cfg:
             # 557 KB is below launch latency: the same operator on one row, timed the same way,
-            # gives the floor of a single timed launch; 100 calls between one pair of events
-            # give the per-call cost once launches overlap.
+            # gives the floor of a single timed launch.
             x1 = x[:1, :1, :1].contiguous()
             c1, s1 = cos[:1].contiguous(), sin[:1].contiguous()
             ent["one_row_launch_ms"] = _median_ms(torch, lambda: T.rmsnorm_rope(x1, w, c1, s1), 20, 5, flush)
-
-            def hundred():
-                for _ in range(100):
-                    T.rmsnorm_rope(x, w, cos, sin)
-
-            ent["per_call_ms_100_back_to_back"] = _median_ms(torch, hundred, 5, 2, flush) / 100
             hx, hw, hc, hs = (_pinned_like(torch, t_) for t_ in (x, w, cos, sin))
             hout = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
             dx, dw, dc, ds = (torch.empty_like(t_) for t_ in (x, w, cos, sin))
