@@ -211,7 +211,9 @@ TLLM_API int tllm_swiglu_colshard(const void *x, const void *w1, const void *w3,
  *   tllm_debug_status (TLLM_DEV_WAIT_TIMEOUT + 5 or + 6) instead of hanging.
  *   variant: 0 automatic (the CTA-pair kernel with tensor stores from M >= 256 when N % 128
  *   == 0 and ldo, N and the buffers allow 16-byte-aligned slices), 1 the one-CTA kernel,
- *   2 the CTA-pair kernel. ndst <= 8; K, N and the leading dimensions multiples of 8.
+ *   2 the CTA-pair kernel, 3 the CTA-pair kernel storing each row as one 256-byte span (3-D
+ *   boxes); all give the same result. ndst <= 8; K, N and the leading dimensions multiples
+ *   of 8.
  */
 TLLM_API int tllm_swiglu_colshard_peers(const void *x, const void *w1, const void *w3,
                                         void *const *dsts, uint32_t *const *flags, int ndst,
