@@ -93,6 +93,30 @@ def test_extension_entries_validate_arguments():
     assert lib.tllm_copy2d_async(None, 0, None, 0, 0, 0, None) == 0  # nothing to copy
 
 
+def test_column_sharded_entry_validates_before_any_launch():
+    """Argument errors of the in-kernel-handshake entry are reported without touching a GPU:
+    a rank outside the group, epoch 0 (the flags' initial value), more than 8 destinations,
+    a row stride that cannot hold every rank's slice, a variant that does not exist."""
+    import ctypes
+
+    lib = _lib.load()
+    vp = ctypes.c_void_p
+    d2 = (vp * 2)(16, 32)
+    done = vp(48)
+
+    def call(dsts, flags, ndst, rank, epoch, ldo, variant=0, m=256, n=128, k=64):
+        return lib.tllm_swiglu_colshard_peers(16, 16, 16, dsts, flags, ndst, rank, done, epoch, m,
+                                              n, k, k, n, n, ldo, 0, variant, None)
+
+    assert call(d2, d2, 2, 2, 1, 256) == 1 and b"rank 2" in lib.tllm_last_error()
+    assert call(d2, d2, 2, 0, 0, 256) == 1 and b"epoch 0" in lib.tllm_last_error()
+    d9 = (vp * 9)(*([16] * 9))
+    assert call(d9, d9, 9, 0, 1, 2048) == 1 and b"destinations" in lib.tllm_last_error()
+    assert call(d2, d2, 2, 1, 1, 200) == 1 and b"row stride" in lib.tllm_last_error()
+    assert call(d2, d2, 2, 0, 1, 256, variant=4) == 1 and b"variant 4" in lib.tllm_last_error()
+    assert call(d2, d2, 2, 0, 1, 256, m=0) == 1 and b"positive" in lib.tllm_last_error()
+
+
 def test_errors_are_thread_local():
     import threading
 

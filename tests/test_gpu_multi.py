@@ -161,3 +161,76 @@ def test_sharded_operators(cuda_device, world):
         assert p.exitcode == 0
     bad = {(r, k): v for r, d in res.items() for k, v in d.items() if v is not True}
     assert not bad, bad
+
+
+def _worker_missing_peer(rank, world, port, q):
+    import datetime
+    import time
+
+    import torch.distributed as dist
+
+    from tritonllmcompiler_b200 import _lib
+    from tritonllmcompiler_b200 import sharded as S
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        import tritonllmcompiler_b200 as T
+
+        m, k, n_loc = 512, 256, 256
+        n = n_loc * world
+        g = torch.Generator(device="cuda").manual_seed(3)
+        x = torch.randn(m, k, generator=g, device="cuda").half()
+        w1 = (torch.randn(k, n, generator=g, device="cuda") / math.sqrt(k)).half()
+        w3 = (torch.randn(k, n, generator=g, device="cuda") / math.sqrt(k)).half()
+        n0, n1 = S.column_range(n, rank, world)
+        w1l, w3l = w1[:, n0:n1].contiguous(), w3[:, n0:n1].contiguous()
+        full = T.swiglu(x, w1, w3)
+        peers = S.PeerBuffers((m, n), x.dtype, x.device)
+        out = S.swiglu_column_sharded(x, w1l, w3l, peers=peers)
+        torch.cuda.synchronize()
+        res = {"healthy call": bool(torch.equal(out, full)), "status clean": _lib.debug_status() == 0}
+        dist.barrier()
+        if rank == 0:
+            # Rank 1 skips this call: rank 0's kernel must give up on its peer (bounded waits)
+            # and report it, not hang.
+            t0 = time.time()
+            S.swiglu_column_sharded(x, w1l, w3l, peers=peers)
+            torch.cuda.synchronize()
+            res["gave up within 30 s"] = time.time() - t0 < 30
+            res["timeout reported"] = (_lib.debug_status() & 0xF00) == 0x100
+            res["context still usable"] = bool(torch.equal(T.swiglu(x, w1, w3), full))
+        dist.barrier()
+        peers.close()
+        q.put((rank, res))
+        dist.barrier()
+    except Exception as e:
+        q.put((rank, {"exception": repr(e)}))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_that_never_launches_is_reported(cuda_device):
+    """A rank that skips a column-sharded call (the failure is made on the host) leaves its
+    peer's kernel waiting on flags that nobody sets: the waits are bounded, the kernel returns,
+    the timeout is reported through the device status word and the context keeps working."""
+    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker_missing_peer, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    bad = {(r, k): v for r, d in res.items() for k, v in d.items() if v is not True}
+    assert not bad, bad
+    assert "timeout reported" in res[0]
