@@ -181,9 +181,13 @@ def test_prefill_split_kv_long_context(cuda_device):
 @pytest.mark.parametrize("lens,hkv,g,d,dtype", [([8000, 2500], 1, 4, 128, torch.float16),   # splits
                                                 ([300, 1, 77, 4096], 2, 8, 64, torch.float16),
                                                 ([513, 900], 4, 2, 128, torch.bfloat16),
+                                                ([0, 40, 7000], 2, 4, 128, torch.float16),
+                                                ([1, 2, 3000], 8, 4, 64, torch.bfloat16),
                                                 ([5000, 33, 0], 3, 5, 128, torch.float16)])
 def test_gqa_single_token_decode(cuda_device, lens, hkv, g, d, dtype):
-    # One new token per sequence and several query heads per KV head.
+    # One new token per sequence and several query heads per KV head: with 2, 4 or 8 query heads
+    # per KV head and D 64 or 128 the CUDA-core grouped-query kernel, otherwise the tensor-core
+    # kernel (5 heads per KV head); an empty context gives NaN as in the reference.
     q, kc, vc, bt, cl = _prefill_case(sum(lens) + g, lens, hkv, g, 1, d, 16, dtype)
     _prefill_check(q, kc, vc, bt, cl, 16)
 

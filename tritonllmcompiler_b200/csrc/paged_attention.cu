@@ -336,6 +336,397 @@ int run(const Params &p, int dtype, cudaStream_t st) {
   return launch_dtype<__nv_bfloat16>(p, st);
 }
 
+namespace {
+template <typename T>
+int launch_merge(const Params &p, cudaStream_t st) {
+  dim3 mgrid(static_cast<unsigned>(p.H), static_cast<unsigned>(p.B));
+  switch (p.D) {
+    case 16: paged_merge_kernel<T, 16><<<mgrid, 16, 0, st>>>(p); break;
+    case 32: paged_merge_kernel<T, 32><<<mgrid, 32, 0, st>>>(p); break;
+    case 64: paged_merge_kernel<T, 64><<<mgrid, 64, 0, st>>>(p); break;
+    default: paged_merge_kernel<T, 128><<<mgrid, 128, 0, st>>>(p); break;
+  }
+  return cuda_status(cudaGetLastError(), "paged merge launch");
+}
+}  // namespace
+
+int run_merge(const Params &p, int dtype, cudaStream_t st) {
+  if (dtype == TLLM_DTYPE_F16) return launch_merge<__half>(p, st);
+  return launch_merge<__nv_bfloat16>(p, st);
+}
+
+// ---------------------------------------------------------------------------------------
+// Grouped-query decode: one CTA per (split, KV head, sequence) computes the G query heads
+// that share the KV head, so every token's K and V rows cross HBM once for all of them.
+//   Loads: the split's K tiles and then its V tiles stream through a ring of kGqaStages
+//   8 KB tiles in shared memory with 16-byte cp.async copies (consecutive threads copy
+//   consecutive 16-byte pieces of one token row; tokens past the context are zero-filled).
+//   The copies hold no registers, so three tiles per CTA stay in flight, and the first
+//   V tiles are already on their way while the split's softmax is taken.
+//   Q.K and P.V: warp-level m16n8k16 MMAs with fp32 accumulation, the G heads as rows 0..G-1
+//   of A (q, exact in registers; p rounded to the input type as in the flash kernels) and K / V
+//   read from the ring by ldmatrix. At up to 8 useful rows of 16 the tensor cores do little
+//   useful work, but the loop then issues about a quarter of the instructions of the same
+//   products on the CUDA cores, which were issue-bound at half of HBM bandwidth.
+// ---------------------------------------------------------------------------------------
+namespace {
+
+constexpr int kGqaStages = 4;
+constexpr int kGqaTileBytes = 8192;
+
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *src, int src_bytes) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// mma.sync m16n8k16 with fp32 accumulation where rows 8-15 of A are zero (a1 = a3 = 0): the
+// G <= 8 query heads of a group occupy rows 0..G-1. The warp-level MMA is used here to cut the
+// instruction count of a memory-bound loop, not for tensor throughput.
+template <typename T>
+struct MmaRows8;
+template <>
+struct MmaRows8<__half> {
+  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0,
+                                             uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+  }
+};
+template <>
+struct MmaRows8<__nv_bfloat16> {
+  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0,
+                                             uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+  }
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a)
+               : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void *p) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a)
+               : "memory");
+}
+
+// Byte offset of 16-byte chunk c of token row r inside a tile: rows of 2*D bytes, chunks
+// XOR-swizzled by the row's low three bits so that the eight rows one ldmatrix reads at the
+// same logical chunk fall into eight different bank groups.
+template <int D>
+__device__ __forceinline__ int tile_off(int r, int c) {
+  return r * (2 * D) + ((c ^ (r & 7)) << 4);
+}
+
+template <typename T, int D, int G>
+__global__ void __launch_bounds__(kThreads, 4) paged_gqa_split_kernel(const Params p) {
+  constexpr int NV = D / 8;                      // 16-byte chunks per token row
+  constexpr int TT = kGqaTileBytes / (2 * D);    // tokens per tile: 32 (D 128) or 64 (D 64)
+  constexpr int TILE_VEC = TT * NV;
+  constexpr int CPT = TILE_VEC / kThreads;       // copies per thread per tile
+  constexpr int KS = D / 16;                     // k-steps of Q.K
+  constexpr int QK_NT = TT / (8 * kWarps);       // 8-token n-tiles per warp in Q.K
+  constexpr int PV_NT = D / (8 * kWarps);        // 8-column n-tiles per warp in P.V
+  constexpr int PV_KS = TT / 16;                 // k-steps of P.V per tile
+  static_assert(TILE_VEC % kThreads == 0 && NV >= 8 && G <= 8, "tile shape");
+  static_assert(QK_NT >= 1 && KS % 2 == 0 && PV_NT % 2 == 0, "fragment shape");
+  extern __shared__ __align__(128) unsigned char smem[];
+  unsigned char *ring = smem;                                                        // [S][TT][2D]
+  float *scores = reinterpret_cast<float *>(smem + kGqaStages * kGqaTileBytes);     // [G][chunk]
+  // Byte offsets within the caches: [0] K, [1] V; per block of the split and per row of a block.
+  int64_t *s_boff = reinterpret_cast<int64_t *>(scores + G * p.chunk);             // [2][chunk / 16]
+  int64_t *s_roff = s_boff + 2 * (p.chunk / 16);                                    // [2][block_size]
+  __shared__ float s_part[G][kWarps];
+  __shared__ float s_m[G], s_l[G];
+
+  const int split = blockIdx.x;
+  const int hk = blockIdx.y;
+  const int b = blockIdx.z;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int r0 = lane >> 2;  // fragment row of this lane = query head within the group
+  const int cq = lane & 3;
+  const bool row_ok = r0 < G;
+
+  int len = __ldg(p.context_lens + b);
+  len = min(len, p.max_tokens);
+  len = max(len, 0);
+  const int t0 = split * p.chunk;
+  if (split > 0 && t0 >= len) return;  // split 0 always runs so an empty context gives NaN
+  const int n = min(len - t0, p.chunk) > 0 ? min(len - t0, p.chunk) : 0;
+
+  // The split's blocks (the chunk is a multiple of the block size) and the rows of a block.
+  const int nblk = (n + p.block_size - 1) >> p.log2_bs;
+  const int nbs = p.chunk / 16;
+  const int32_t *bt = p.block_tables + b * p.sbt0;
+  const int64_t kv_off = hk * p.skc2 * static_cast<int64_t>(sizeof(T));
+  const int64_t vv_off = hk * p.svc2 * static_cast<int64_t>(sizeof(T));
+  for (int i = tid; i < nblk; i += kThreads) {
+    const int64_t phys = checked_block(bt, ((t0 >> p.log2_bs) + i) * p.sbt1, p.num_blocks);
+    s_boff[i] = phys * p.skc0 * static_cast<int64_t>(sizeof(T)) + kv_off;
+    s_boff[nbs + i] = phys * p.svc0 * static_cast<int64_t>(sizeof(T)) + vv_off;
+  }
+  for (int i = tid; i < p.block_size; i += kThreads) {
+    s_roff[i] = i * p.skc1 * static_cast<int64_t>(sizeof(T));
+    s_roff[p.block_size + i] = i * p.svc1 * static_cast<int64_t>(sizeof(T));
+  }
+
+  // A fragments of q (the raw input elements; the scale is applied to the fp32 scores).
+  uint32_t qa[KS][2];
+  {
+    const uint16_t *qp = static_cast<const uint16_t *>(p.q) + b * p.sq0 + (hk * G + (row_ok ? r0 : 0)) * p.sq1;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int d0 = 16 * ks + 8 * h + 2 * cq;
+        qa[ks][h] = row_ok ? (static_cast<uint32_t>(qp[d0 * p.sq3]) |
+                              (static_cast<uint32_t>(qp[(d0 + 1) * p.sq3]) << 16))
+                           : 0u;
+      }
+  }
+  __syncthreads();
+
+  const int nt = (n + TT - 1) / TT;
+  const int total = 2 * nt;  // K tiles, then V tiles
+  // This thread copies chunk c of rows r_i = tid / NV + i * (kThreads / NV) of every tile, to
+  // fixed places in the tile.
+  const int c = tid % NV;
+  const char *ksrc = static_cast<const char *>(p.k_cache) + c * 16;
+  const char *vsrc = static_cast<const char *>(p.v_cache) + c * 16;
+
+  auto issue = [&](int j) {
+    if (j < total) {
+      const int isv = j >= nt;
+      const int tb = (isv ? j - nt : j) * TT;
+      const int64_t *boff = s_boff + isv * nbs;
+      const int64_t *roff = s_roff + isv * p.block_size;
+      const char *base = isv ? vsrc : ksrc;
+      unsigned char *dst = ring + (j % kGqaStages) * kGqaTileBytes;
+#pragma unroll
+      for (int i = 0; i < CPT; ++i) {
+        const int row = tid / NV + i * (kThreads / NV);
+        const int tl = tb + row;
+        const char *src = base;
+        int bytes = 0;
+        if (tl < n) {
+          src = base + boff[tl >> p.log2_bs] + roff[tl & (p.block_size - 1)];
+          bytes = 16;
+        }
+        cp_async16(dst + tile_off<D>(row, c), src, bytes);
+      }
+    }
+    cp_async_commit();  // empty groups past the end keep the group count uniform
+  };
+
+#pragma unroll
+  for (int j = 0; j < kGqaStages - 1; ++j) issue(j);
+
+  // ---- scores: S[head][token] = q . k on the tensor cores, one 8-token n-tile per warp step ----
+  const float qscale = p.sm_scale * kLog2e;
+  float mloc = -INFINITY;
+  for (int j = 0; j < nt; ++j) {
+    cp_async_wait<kGqaStages - 2>();
+    __syncthreads();  // tile j landed for every thread; tile j - 1's slot is free
+    issue(j + kGqaStages - 1);
+    const unsigned char *tile = ring + (j % kGqaStages) * kGqaTileBytes;
+#pragma unroll
+    for (int q = 0; q < QK_NT; ++q) {
+      const int tok0 = (warp * QK_NT + q) * 8;
+      float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int kp = 0; kp < KS / 2; ++kp) {
+        uint32_t bf[4];
+        const int row = tok0 + (lane & 7);
+        ldsm_x4(bf, tile + tile_off<D>(row, 4 * kp + (lane >> 3)));
+        MmaRows8<T>::run(c, qa[2 * kp][0], qa[2 * kp][1], bf[0], bf[1]);
+        MmaRows8<T>::run(c, qa[2 * kp + 1][0], qa[2 * kp + 1][1], bf[2], bf[3]);
+      }
+      if (row_ok) {
+        const int tl = j * TT + tok0 + 2 * cq;
+        const float s0 = c[0] * qscale, s1 = c[1] * qscale;
+        if (tl < n) mloc = fmaxf(mloc, s0);
+        if (tl + 1 < n) mloc = fmaxf(mloc, s1);
+        *reinterpret_cast<float2 *>(scores + r0 * p.chunk + tl) = make_float2(s0, s1);
+      }
+    }
+  }
+
+  // ---- softmax over the split's scores, per head: max, p = exp2(s - max) in place (0 past the
+  // context, up to the last tile's end), sum. With an empty context the sum is 0, so the output
+  // is NaN as in the reference. ----
+  mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 1));
+  mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 2));
+  if (row_ok && cq == 0) s_part[r0][warp] = mloc;
+  __syncthreads();
+  float m[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = s_part[g][0];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) m[g] = fmaxf(m[g], s_part[g][w]);
+  }
+  if (tid < G) {
+    float mm = s_part[tid][0];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) mm = fmaxf(mm, s_part[tid][w]);
+    s_m[tid] = mm;
+  }
+  __syncthreads();  // s_part is reused for the sums
+  const int npad = nt * TT;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float l = 0.f;
+    for (int i = tid; i < npad; i += kThreads) {
+      const float e = i < n ? exp2f(scores[g * p.chunk + i] - m[g]) : 0.f;
+      scores[g * p.chunk + i] = e;
+      l += e;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+    if (lane == 0) s_part[g][warp] = l;
+  }
+  __syncthreads();
+  if (tid < G) {
+    float l = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) l += s_part[tid][w];
+    s_l[tid] = l;
+  }
+
+  // ---- O[head][d] += P . V on the tensor cores; each warp owns D/4 output columns ----
+  float acc[PV_NT][4];
+#pragma unroll
+  for (int q = 0; q < PV_NT; ++q)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[q][i] = 0.f;
+  for (int j = nt; j < total; ++j) {
+    cp_async_wait<kGqaStages - 2>();
+    __syncthreads();
+    issue(j + kGqaStages - 1);
+    const unsigned char *tile = ring + (j % kGqaStages) * kGqaTileBytes;
+    const float *prow = scores + r0 * p.chunk + (j - nt) * TT + 2 * cq;
+#pragma unroll
+    for (int ks = 0; ks < PV_KS; ++ks) {
+      uint32_t pa0 = 0u, pa2 = 0u;
+      if (row_ok) {
+        const float2 x = *reinterpret_cast<const float2 *>(prow + 16 * ks);
+        const float2 y = *reinterpret_cast<const float2 *>(prow + 16 * ks + 8);
+        pa0 = Pack2<T>::pack(x.x, x.y);
+        pa2 = Pack2<T>::pack(y.x, y.y);
+      }
+      const int row = 16 * ks + 8 * ((lane >> 3) & 1) + (lane & 7);
+#pragma unroll
+      for (int np = 0; np < PV_NT / 2; ++np) {
+        uint32_t bf[4];
+        ldsm_x4_trans(bf, tile + tile_off<D>(row, warp * PV_NT + 2 * np + (lane >> 4)));
+        MmaRows8<T>::run(acc[2 * np], pa0, pa2, bf[0], bf[1]);
+        MmaRows8<T>::run(acc[2 * np + 1], pa0, pa2, bf[2], bf[3]);
+      }
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();  // s_l is visible (also with no tiles)
+
+  if (row_ok) {
+    const int h = hk * G + r0;
+    const float inv_l = 1.f / s_l[r0];
+    const int64_t slot = (static_cast<int64_t>(b) * p.H + h) * p.num_splits + split;
+#pragma unroll
+    for (int q = 0; q < PV_NT; ++q) {
+      const int d = (warp * PV_NT + q) * 8 + 2 * cq;
+      if (p.num_splits == 1) {
+        T *op = static_cast<T *>(p.o) + b * p.so0 + h * p.so1;
+        op[d * p.so3] = from_f32<T>(acc[q][0] * inv_l);
+        op[(d + 1) * p.so3] = from_f32<T>(acc[q][1] * inv_l);
+      } else {
+        *reinterpret_cast<float2 *>(p.ws_acc + slot * D + d) = make_float2(acc[q][0], acc[q][1]);
+      }
+    }
+    if (p.num_splits > 1 && warp == 0 && cq == 0) {
+      p.ws_ml[2 * slot] = s_m[r0];
+      p.ws_ml[2 * slot + 1] = s_l[r0];
+    }
+  }
+}
+
+// Ring, scores of the G heads, and the K and V byte offsets of the split's blocks (block
+// size >= 16) and of the rows of a block (block size <= 64).
+size_t gqa_smem_bytes(int64_t G, int64_t chunk) {
+  return static_cast<size_t>(kGqaStages) * kGqaTileBytes +
+         static_cast<size_t>(G * chunk) * sizeof(float) +
+         static_cast<size_t>(2 * (chunk / 16) + 2 * 64) * sizeof(int64_t);
+}
+
+template <typename T, int D, int G>
+int launch_gqa_typed(const Params &p, cudaStream_t st) {
+  const size_t smem = gqa_smem_bytes(G, p.chunk);
+  auto kern = paged_gqa_split_kernel<T, D, G>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(paged gqa split)");
+  }
+  dim3 grid(p.num_splits, static_cast<unsigned>(p.Hkv), static_cast<unsigned>(p.B));
+  kern<<<grid, kThreads, smem, st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_status(e, "paged gqa split launch");
+  if (p.num_splits > 1) return launch_merge<T>(p, st);
+  return TLLM_OK;
+}
+
+template <typename T, int D>
+int launch_gqa_d(const Params &p, cudaStream_t st) {
+  switch (p.G) {
+    case 2: return launch_gqa_typed<T, D, 2>(p, st);
+    case 4: return launch_gqa_typed<T, D, 4>(p, st);
+    default: return launch_gqa_typed<T, D, 8>(p, st);
+  }
+}
+
+}  // namespace
+
+Plan plan_gqa(int64_t B, int64_t H, int64_t Hkv, int64_t D, int64_t block_size,
+              int64_t max_blocks, int sms) {
+  Plan pl = plan(B, Hkv, D, block_size, max_blocks, sms);
+  if (pl.num_splits > 1) {
+    pl.ws_ml_floats = B * H * pl.num_splits * 2;
+    pl.ws_acc_floats = B * H * pl.num_splits * D;
+  }
+  const size_t ml_bytes = ((pl.ws_ml_floats * sizeof(float)) + 255) / 256 * 256;
+  pl.ws_bytes = ml_bytes + pl.ws_acc_floats * sizeof(float);
+  pl.ws_acc_offset = ml_bytes;
+  return pl;
+}
+
+bool gqa_supported(int64_t G, int64_t D, const Plan &pl) {
+  return (G == 2 || G == 4 || G == 8) && (D == 64 || D == 128) &&
+         gqa_smem_bytes(G, pl.chunk) <= 200 * 1024;
+}
+
+int run_gqa(const Params &p, int dtype, cudaStream_t st) {
+  if (dtype == TLLM_DTYPE_F16)
+    return p.D == 64 ? launch_gqa_d<__half, 64>(p, st) : launch_gqa_d<__half, 128>(p, st);
+  return p.D == 64 ? launch_gqa_d<__nv_bfloat16, 64>(p, st) : launch_gqa_d<__nv_bfloat16, 128>(p, st);
+}
+
 }  // namespace paged
 }  // namespace tllm
 

@@ -29,6 +29,10 @@ struct Params {
   int64_t sbt0, sbt1;
   int64_t so0, so1, so3;
   float sm_scale;
+  // Grouped-query decode (run_gqa): query heads per KV head and the number of KV heads; the
+  // caches' head index is the KV head, q / o / the workspace use the H = G * Hkv query heads.
+  int G = 1;
+  int64_t Hkv = 0;
 };
 
 struct Plan {
@@ -50,6 +54,17 @@ int validate(const Params &p);
 int read_status(int *out);
 // Enqueues the split kernel (and the merge kernel when num_splits > 1).
 int run(const Params &p, int dtype, cudaStream_t st);
+// Enqueues the merge of the split partials into o for the p.H heads.
+int run_merge(const Params &p, int dtype, cudaStream_t st);
+
+// Single-token decode with G = H / Hkv query heads per KV head on the CUDA cores: each token's
+// K and V rows are read once for all G heads. The plan is made over the KV heads; its
+// workspace holds the partials of all H query heads.
+Plan plan_gqa(int64_t B, int64_t H, int64_t Hkv, int64_t D, int64_t block_size,
+              int64_t max_blocks, int sms);
+// Whether run_gqa handles this group size, head dim and plan (otherwise use another path).
+bool gqa_supported(int64_t G, int64_t D, const Plan &pl);
+int run_gqa(const Params &p, int dtype, cudaStream_t st);
 
 }  // namespace paged
 }  // namespace tllm

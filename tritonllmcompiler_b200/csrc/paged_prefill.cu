@@ -648,11 +648,18 @@ namespace ppf {
 namespace {
 // Single-token decode with one query head per KV head is the reference's decode: it goes to
 // the CUDA-core split-KV kernel, which reads each token's K/V row with vector loads (this
-// kernel is bound by TMA box issue on paged blocks and reaches less there; with several query
-// heads per KV head the tensor-core path here is the faster one).
+// kernel is bound by TMA box issue on paged blocks and reaches less there).
 bool use_decode_path(int64_t Hq, int64_t Hkv, int64_t Sq, int64_t D) {
   (void)D;
   return Sq == 1 && Hq == Hkv;
+}
+// Single-token decode with 2, 4 or 8 query heads per KV head (D 64 or 128) goes to the
+// CUDA-core grouped-query split kernel, which reads each token's K/V rows once for the group.
+bool use_gqa_decode_path(int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t D,
+                         int64_t block_size, int64_t max_blocks) {
+  if (Sq != 1 || Hq == Hkv) return false;
+  const paged::Plan pl = paged::plan_gqa(B, Hq, Hkv, D, block_size, max_blocks, sm_count());
+  return paged::gqa_supported(Hq / Hkv, D, pl);
 }
 }  // namespace
 }  // namespace ppf
@@ -666,6 +673,8 @@ extern "C" size_t tllm_paged_prefill_workspace_size(int64_t B, int64_t Hq, int64
     return 0;
   if (tllm::ppf::use_decode_path(Hq, Hkv, Sq, D))
     return tllm::paged::plan(B, Hq, D, block_size, max_blocks, tllm::sm_count()).ws_bytes;
+  if (tllm::ppf::use_gqa_decode_path(B, Hq, Hkv, Sq, D, block_size, max_blocks))
+    return tllm::paged::plan_gqa(B, Hq, Hkv, D, block_size, max_blocks, tllm::sm_count()).ws_bytes;
   return tllm::ppf::make_plan(B, Hq, Hkv, Sq, D, block_size, max_blocks, tllm::sm_count()).ws_bytes;
 }
 
@@ -704,8 +713,10 @@ extern "C" int tllm_paged_prefill(const void *q, const void *k_cache, const void
                    "paged_prefill: q/cache strides must be multiples of 8 elements");
   TLLM_CHECK_ARG(aligned16(q) && aligned16(k_cache) && aligned16(v_cache),
                  "paged_prefill: q and the caches must be 16-byte aligned");
-  if (use_decode_path(Hq, Hkv, Sq, D)) {
-    const paged::Plan dp = paged::plan(B, Hq, D, block_size, max_blocks, sm_count());
+  const bool gqa = use_gqa_decode_path(B, Hq, Hkv, Sq, D, block_size, max_blocks);
+  if (use_decode_path(Hq, Hkv, Sq, D) || gqa) {
+    const paged::Plan dp = gqa ? paged::plan_gqa(B, Hq, Hkv, D, block_size, max_blocks, sm_count())
+                               : paged::plan(B, Hq, D, block_size, max_blocks, sm_count());
     paged::Params p{};
     p.q = q; p.k_cache = k_cache; p.v_cache = v_cache;
     p.block_tables = block_tables; p.context_lens = context_lens; p.o = o;
@@ -722,6 +733,8 @@ extern "C" int tllm_paged_prefill(const void *q, const void *k_cache, const void
     p.sbt0 = sbt[0]; p.sbt1 = sbt[1];
     p.so0 = so[0]; p.so1 = so[1]; p.so3 = so[3];
     p.sm_scale = sm_scale;
+    p.G = static_cast<int>(Hq / Hkv);
+    p.Hkv = Hkv;
     int rc = paged::validate(p);
     if (rc) return rc;
     if (dp.num_splits > 1) {
@@ -733,6 +746,7 @@ extern "C" int tllm_paged_prefill(const void *q, const void *k_cache, const void
       p.ws_ml = static_cast<float *>(workspace);
       p.ws_acc = reinterpret_cast<float *>(static_cast<char *>(workspace) + dp.ws_acc_offset);
     }
+    if (gqa) return paged::run_gqa(p, dtype, static_cast<cudaStream_t>(stream));
     return paged::run(p, dtype, static_cast<cudaStream_t>(stream));
   }
   const Plan pl = make_plan(B, Hq, Hkv, Sq, D, block_size, max_blocks, sm_count());
