@@ -285,9 +285,10 @@ TLLM_API int tllm_paged_kv_append_rope(const void *k_new, const void *v_new, con
  * (strides so). context_lens[b] counts the new tokens (they are already in the cache); query
  * token s sits at position context_lens[b] - Sq + s and, when causal != 0, sees the keys at
  * positions <= its own (all context_lens[b] keys otherwise). A query that sees no key gives
- * NaN. With Sq = 1 and Hq = Hkv this is tllm_paged_attn_decode; with Sq = 1, Hq / Hkv in
- * {2, 4, 8} and D in {64, 128} a grouped-query decode kernel reads each K/V row once for the
- * Hq / Hkv query heads (the workspace size entry accounts for it). Requirements as for
+ * NaN. With Sq = 1 and Hq = Hkv this is tllm_paged_attn_decode; otherwise, with at most 16
+ * query rows per KV head ((Hq / Hkv) * Sq <= 16) and D in {64, 128}, a grouped-query split
+ * kernel reads each K/V row once for those rows (the workspace size entry accounts for it);
+ * larger calls run the tensor-core prefill kernel. Requirements as for
  * tllm_paged_attn_decode (block_size in {16,32,64}, D in {16,32,64,128}, unit inner strides,
  * 16-byte alignment); the workspace (256-byte aligned) holds split-KV partials when a launch
  * splits the keys (tllm_paged_prefill_workspace_size, 0 when it does not).

@@ -160,6 +160,12 @@ def _prefill_check(q, kc, vc, bt, lens, bs, causal=True):
     ([700, 300], 1, 2, 200, 128, 16),           # prefill: two token tiles per head
     ([5, 130, 17], 3, 2, 5, 32, 16),            # short contexts, D 32
     ([64, 1, 3], 2, 1, 3, 16, 16),              # D 16, contexts shorter than the new tokens
+    # at most 16 query rows per KV head (D 64/128): the grouped-query split kernel
+    ([2, 1, 300, 4], 2, 2, 4, 128, 16),         # contexts shorter than the new tokens
+    ([37, 500], 4, 1, 6, 64, 16),               # one head per KV head, 6 new tokens
+    ([100, 2000], 1, 8, 2, 64, 32),             # 16 rows at D 64
+    ([3000, 7000, 20], 2, 16, 1, 128, 16),      # 16 query heads per KV head, one token
+    ([5000, 129], 1, 5, 3, 128, 64),            # 15 rows, split keys
 ])
 def test_prefill_matches_oracle(cuda_device, lens, hkv, g, sq, d, bs):
     q, kc, vc, bt, cl = _prefill_case(sum(lens) + sq, lens, hkv, g, sq, d, bs)
@@ -168,6 +174,11 @@ def test_prefill_matches_oracle(cuda_device, lens, hkv, g, sq, d, bs):
 
 def test_prefill_non_causal_and_bf16(cuda_device):
     q, kc, vc, bt, cl = _prefill_case(3, [150, 900], 2, 3, 6, 128, 16, dtype=torch.bfloat16)
+    _prefill_check(q, kc, vc, bt, cl, 16, causal=False)
+    # 15 and 4 query rows per KV head: the grouped-query split kernel
+    q, kc, vc, bt, cl = _prefill_case(4, [150, 4900, 3], 2, 3, 5, 128, 16, dtype=torch.bfloat16)
+    _prefill_check(q, kc, vc, bt, cl, 16, causal=False)
+    q, kc, vc, bt, cl = _prefill_case(5, [2, 77], 1, 2, 2, 64, 16, dtype=torch.bfloat16)
     _prefill_check(q, kc, vc, bt, cl, 16, causal=False)
 
 
@@ -185,9 +196,9 @@ def test_prefill_split_kv_long_context(cuda_device):
                                                 ([1, 2, 3000], 8, 4, 64, torch.bfloat16),
                                                 ([5000, 33, 0], 3, 5, 128, torch.float16)])
 def test_gqa_single_token_decode(cuda_device, lens, hkv, g, d, dtype):
-    # One new token per sequence and several query heads per KV head: with 2, 4 or 8 query heads
-    # per KV head and D 64 or 128 the CUDA-core grouped-query kernel, otherwise the tensor-core
-    # kernel (5 heads per KV head); an empty context gives NaN as in the reference.
+    # One new token per sequence and several query heads per KV head (the grouped-query split
+    # kernel at D 64 and 128, with 2 to 8 query rows); an empty context gives NaN as in the
+    # reference.
     q, kc, vc, bt, cl = _prefill_case(sum(lens) + g, lens, hkv, g, 1, d, 16, dtype)
     _prefill_check(q, kc, vc, bt, cl, 16)
 

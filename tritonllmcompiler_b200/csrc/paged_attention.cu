@@ -217,17 +217,19 @@ __global__ void __launch_bounds__(kThreads) paged_split_kernel(const Params p) {
   }
 }
 
-// One CTA of D threads per (head, sequence): log-sum-exp merge of the active splits.
+// One CTA of D threads per (head, new token, sequence): log-sum-exp merge of the active splits.
 template <typename T, int D>
 __global__ void __launch_bounds__(D) paged_merge_kernel(const Params p) {
-  const int h = blockIdx.x;
+  const int hs = blockIdx.x;  // head * Sq + new token
+  const int h = hs / p.Sq;
+  const int tok = hs - h * p.Sq;
   const int b = blockIdx.y;
   const int d = threadIdx.x;
   int len = __ldg(p.context_lens + b);
   len = min(len, p.max_tokens);
   len = max(len, 0);
   const int active = len > 0 ? (len + p.chunk - 1) / p.chunk : 1;
-  const int64_t slot0 = (static_cast<int64_t>(b) * p.H + h) * p.num_splits;
+  const int64_t slot0 = (static_cast<int64_t>(b) * p.H * p.Sq + hs) * p.num_splits;
   float M = -INFINITY;
   for (int s = 0; s < active; ++s) M = fmaxf(M, p.ws_ml[2 * (slot0 + s)]);
   float L = 0.f, A = 0.f;
@@ -236,7 +238,7 @@ __global__ void __launch_bounds__(D) paged_merge_kernel(const Params p) {
     L = fmaf(p.ws_ml[2 * (slot0 + s) + 1], wgt, L);
     A = fmaf(p.ws_acc[(slot0 + s) * D + d], wgt, A);
   }
-  T *op = static_cast<T *>(p.o) + b * p.so0 + h * p.so1;
+  T *op = static_cast<T *>(p.o) + b * p.so0 + h * p.so1 + tok * p.so2;
   op[d * p.so3] = from_f32<T>(A / L);
 }
 
@@ -339,7 +341,7 @@ int run(const Params &p, int dtype, cudaStream_t st) {
 namespace {
 template <typename T>
 int launch_merge(const Params &p, cudaStream_t st) {
-  dim3 mgrid(static_cast<unsigned>(p.H), static_cast<unsigned>(p.B));
+  dim3 mgrid(static_cast<unsigned>(p.H * p.Sq), static_cast<unsigned>(p.B));
   switch (p.D) {
     case 16: paged_merge_kernel<T, 16><<<mgrid, 16, 0, st>>>(p); break;
     case 32: paged_merge_kernel<T, 32><<<mgrid, 32, 0, st>>>(p); break;
@@ -357,17 +359,19 @@ int run_merge(const Params &p, int dtype, cudaStream_t st) {
 
 // ---------------------------------------------------------------------------------------
 // Grouped-query decode: one CTA per (split, KV head, sequence) computes the G query heads
-// that share the KV head, so every token's K and V rows cross HBM once for all of them.
+// that share the KV head, for Sq >= 1 new tokens, so every token's K and V rows cross HBM once
+// for all of them.
 //   Loads: the split's K tiles and then its V tiles stream through a ring of kGqaStages
 //   8 KB tiles in shared memory with 16-byte cp.async copies (consecutive threads copy
 //   consecutive 16-byte pieces of one token row; tokens past the context are zero-filled).
 //   The copies hold no registers, so three tiles per CTA stay in flight, and the first
 //   V tiles are already on their way while the split's softmax is taken.
-//   Q.K and P.V: warp-level m16n8k16 MMAs with fp32 accumulation, the G heads as rows 0..G-1
-//   of A (q, exact in registers; p rounded to the input type as in the flash kernels) and K / V
-//   read from the ring by ldmatrix. At up to 8 useful rows of 16 the tensor cores do little
-//   useful work, but the loop then issues about a quarter of the instructions of the same
-//   products on the CUDA cores, which were issue-bound at half of HBM bandwidth.
+//   Q.K and P.V: warp-level m16n8k16 MMAs with fp32 accumulation, the R = G * Sq query rows
+//   (G heads times Sq new tokens, R <= 16) as the rows of A (q, exact in registers; p rounded
+//   to the input type as in the flash kernels) and K / V read from the ring by ldmatrix. With
+//   few useful rows the tensor cores do little useful work, but the loop then issues about a
+//   quarter of the instructions of the same products on the CUDA cores, which were issue-bound
+//   at half of HBM bandwidth. With several new tokens each row has its own causal key limit.
 // ---------------------------------------------------------------------------------------
 namespace {
 
@@ -385,29 +389,29 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// mma.sync m16n8k16 with fp32 accumulation where rows 8-15 of A are zero (a1 = a3 = 0): the
-// G <= 8 query heads of a group occupy rows 0..G-1. The warp-level MMA is used here to cut the
-// instruction count of a memory-bound loop, not for tensor throughput.
+// mma.sync m16n8k16 with fp32 accumulation. The warp-level MMA is used here to cut the
+// instruction count of a memory-bound loop, not for tensor throughput; with at most 8 query
+// rows the caller passes zero for the A registers of rows 8-15 (a1, a3).
 template <typename T>
-struct MmaRows8;
+struct Mma16816;
 template <>
-struct MmaRows8<__half> {
-  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0,
-                                             uint32_t b1) {
+struct Mma16816<__half> {
+  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                             uint32_t a3, uint32_t b0, uint32_t b1) {
     asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
         "{%8, %9}, {%0, %1, %2, %3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
   }
 };
 template <>
-struct MmaRows8<__nv_bfloat16> {
-  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0,
-                                             uint32_t b1) {
+struct Mma16816<__nv_bfloat16> {
+  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                             uint32_t a3, uint32_t b0, uint32_t b1) {
     asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
         "{%8, %9}, {%0, %1, %2, %3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
   }
 };
 
@@ -434,7 +438,18 @@ __device__ __forceinline__ int tile_off(int r, int c) {
   return r * (2 * D) + ((c ^ (r & 7)) << 4);
 }
 
-template <typename T, int D, int G>
+// Number of the split's keys (local index < the result) that query row r may see: all n with
+// causal off; with causal on, query token s of Sq sits at position len - Sq + s and sees the
+// keys at positions <= its own.
+__device__ __forceinline__ int row_key_limit(const Params &p, int r, int len, int t0, int n) {
+  if (!p.causal) return n;
+  const int s = r % p.Sq;
+  return min(max(len - p.Sq + s + 1 - t0, 0), n);
+}
+
+// R = G * Sq query rows (row r = g * Sq + s: query head hk * G + g, new token s); kR16: rows 8-15
+// are in use.
+template <typename T, int D, bool kR16>
 __global__ void __launch_bounds__(kThreads, 4) paged_gqa_split_kernel(const Params p) {
   constexpr int NV = D / 8;                      // 16-byte chunks per token row
   constexpr int TT = kGqaTileBytes / (2 * D);    // tokens per tile: 32 (D 128) or 64 (D 64)
@@ -444,16 +459,22 @@ __global__ void __launch_bounds__(kThreads, 4) paged_gqa_split_kernel(const Para
   constexpr int QK_NT = TT / (8 * kWarps);       // 8-token n-tiles per warp in Q.K
   constexpr int PV_NT = D / (8 * kWarps);        // 8-column n-tiles per warp in P.V
   constexpr int PV_KS = TT / 16;                 // k-steps of P.V per tile
-  static_assert(TILE_VEC % kThreads == 0 && NV >= 8 && G <= 8, "tile shape");
+  static_assert(TILE_VEC % kThreads == 0 && NV >= 8, "tile shape");
   static_assert(QK_NT >= 1 && KS % 2 == 0 && PV_NT % 2 == 0, "fragment shape");
+  constexpr int TPR = kR16 ? 8 : 16;             // softmax threads per query row
   extern __shared__ __align__(128) unsigned char smem[];
   unsigned char *ring = smem;                                                        // [S][TT][2D]
-  float *scores = reinterpret_cast<float *>(smem + kGqaStages * kGqaTileBytes);     // [G][chunk]
+  // Scores [R][SST]: rows padded by TPR floats, so the TPR-thread groups of the softmax that
+  // share a warp read different banks.
+  const int SST = p.chunk + TPR;
+  float *scores = reinterpret_cast<float *>(smem + kGqaStages * kGqaTileBytes);
+  const int R = p.G * p.Sq;
   // Byte offsets within the caches: [0] K, [1] V; per block of the split and per row of a block.
-  int64_t *s_boff = reinterpret_cast<int64_t *>(scores + G * p.chunk);             // [2][chunk / 16]
+  int64_t *s_boff = reinterpret_cast<int64_t *>(scores + R * SST);                 // [2][chunk / 16]
   int64_t *s_roff = s_boff + 2 * (p.chunk / 16);                                    // [2][block_size]
-  __shared__ float s_part[G][kWarps];
-  __shared__ float s_m[G], s_l[G];
+  __shared__ float s_part[16][kWarps];
+  __shared__ float s_m[16], s_l[16];
+  __shared__ int s_lim[16];
 
   const int split = blockIdx.x;
   const int hk = blockIdx.y;
@@ -461,9 +482,11 @@ __global__ void __launch_bounds__(kThreads, 4) paged_gqa_split_kernel(const Para
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const int r0 = lane >> 2;  // fragment row of this lane = query head within the group
+  const int r0 = lane >> 2;  // fragment rows of this lane: r0 and r0 + 8
+  const int r1 = r0 + 8;
   const int cq = lane & 3;
-  const bool row_ok = r0 < G;
+  const bool ok0 = r0 < R;
+  const bool ok1 = kR16 && r1 < R;
 
   int len = __ldg(p.context_lens + b);
   len = min(len, p.max_tokens);
@@ -487,27 +510,40 @@ __global__ void __launch_bounds__(kThreads, 4) paged_gqa_split_kernel(const Para
     s_roff[i] = i * p.skc1 * static_cast<int64_t>(sizeof(T));
     s_roff[p.block_size + i] = i * p.svc1 * static_cast<int64_t>(sizeof(T));
   }
+  if (tid < R) s_lim[tid] = row_key_limit(p, tid, len, t0, n);
 
-  // A fragments of q (the raw input elements; the scale is applied to the fp32 scores).
-  uint32_t qa[KS][2];
+  // A fragments of q (the raw input elements; the scale is applied to the fp32 scores):
+  // qa[ks][0] = a0 (row r0), [1] = a2 (row r0, upper 8 columns), [2] = a1 (row r1), [3] = a3.
+  uint32_t qa[KS][kR16 ? 4 : 2];
   {
-    const uint16_t *qp = static_cast<const uint16_t *>(p.q) + b * p.sq0 + (hk * G + (row_ok ? r0 : 0)) * p.sq1;
+    auto qrow = [&](int r) {
+      return static_cast<const uint16_t *>(p.q) + b * p.sq0 + (hk * p.G + r / p.Sq) * p.sq1 +
+             (r % p.Sq) * p.sq2;
+    };
+    const uint16_t *q0 = qrow(ok0 ? r0 : 0);
+    const uint16_t *q1 = qrow(ok1 ? r1 : 0);
 #pragma unroll
     for (int ks = 0; ks < KS; ++ks)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int d0 = 16 * ks + 8 * h + 2 * cq;
-        qa[ks][h] = row_ok ? (static_cast<uint32_t>(qp[d0 * p.sq3]) |
-                              (static_cast<uint32_t>(qp[(d0 + 1) * p.sq3]) << 16))
-                           : 0u;
+        qa[ks][h] = ok0 ? (static_cast<uint32_t>(q0[d0 * p.sq3]) |
+                           (static_cast<uint32_t>(q0[(d0 + 1) * p.sq3]) << 16))
+                        : 0u;
+        if constexpr (kR16)
+          qa[ks][2 + h] = ok1 ? (static_cast<uint32_t>(q1[d0 * p.sq3]) |
+                                 (static_cast<uint32_t>(q1[(d0 + 1) * p.sq3]) << 16))
+                              : 0u;
       }
   }
   __syncthreads();
+  const int lim0 = ok0 ? s_lim[r0] : 0;
+  const int lim1 = ok1 ? s_lim[r1] : 0;
 
   const int nt = (n + TT - 1) / TT;
   const int total = 2 * nt;  // K tiles, then V tiles
-  // This thread copies chunk c of rows r_i = tid / NV + i * (kThreads / NV) of every tile, to
-  // fixed places in the tile.
+  // This thread copies chunk c of rows tid / NV + i * (kThreads / NV) of every tile, to fixed
+  // places in the tile.
   const int c = tid % NV;
   const char *ksrc = static_cast<const char *>(p.k_cache) + c * 16;
   const char *vsrc = static_cast<const char *>(p.v_cache) + c * 16;
@@ -539,9 +575,9 @@ __global__ void __launch_bounds__(kThreads, 4) paged_gqa_split_kernel(const Para
 #pragma unroll
   for (int j = 0; j < kGqaStages - 1; ++j) issue(j);
 
-  // ---- scores: S[head][token] = q . k on the tensor cores, one 8-token n-tile per warp step ----
+  // ---- scores: S[row][token] = q . k on the tensor cores, one 8-token n-tile per warp step ----
   const float qscale = p.sm_scale * kLog2e;
-  float mloc = -INFINITY;
+  float mloc0 = -INFINITY, mloc1 = -INFINITY;
   for (int j = 0; j < nt; ++j) {
     cp_async_wait<kGqaStages - 2>();
     __syncthreads();  // tile j landed for every thread; tile j - 1's slot is free
@@ -550,68 +586,78 @@ __global__ void __launch_bounds__(kThreads, 4) paged_gqa_split_kernel(const Para
 #pragma unroll
     for (int q = 0; q < QK_NT; ++q) {
       const int tok0 = (warp * QK_NT + q) * 8;
-      float c[4] = {0.f, 0.f, 0.f, 0.f};
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int kp = 0; kp < KS / 2; ++kp) {
         uint32_t bf[4];
         const int row = tok0 + (lane & 7);
         ldsm_x4(bf, tile + tile_off<D>(row, 4 * kp + (lane >> 3)));
-        MmaRows8<T>::run(c, qa[2 * kp][0], qa[2 * kp][1], bf[0], bf[1]);
-        MmaRows8<T>::run(c, qa[2 * kp + 1][0], qa[2 * kp + 1][1], bf[2], bf[3]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int ks = 2 * kp + h;
+          if constexpr (kR16)
+            Mma16816<T>::run(acc, qa[ks][0], qa[ks][2], qa[ks][1], qa[ks][3], bf[2 * h], bf[2 * h + 1]);
+          else
+            Mma16816<T>::run(acc, qa[ks][0], 0u, qa[ks][1], 0u, bf[2 * h], bf[2 * h + 1]);
+        }
       }
-      if (row_ok) {
-        const int tl = j * TT + tok0 + 2 * cq;
-        const float s0 = c[0] * qscale, s1 = c[1] * qscale;
-        if (tl < n) mloc = fmaxf(mloc, s0);
-        if (tl + 1 < n) mloc = fmaxf(mloc, s1);
-        *reinterpret_cast<float2 *>(scores + r0 * p.chunk + tl) = make_float2(s0, s1);
+      const int tl = j * TT + tok0 + 2 * cq;
+      if (ok0) {
+        const float s0 = acc[0] * qscale, s1 = acc[1] * qscale;
+        if (tl < lim0) mloc0 = fmaxf(mloc0, s0);
+        if (tl + 1 < lim0) mloc0 = fmaxf(mloc0, s1);
+        *reinterpret_cast<float2 *>(scores + r0 * SST + tl) = make_float2(s0, s1);
+      }
+      if (ok1) {
+        const float s0 = acc[2] * qscale, s1 = acc[3] * qscale;
+        if (tl < lim1) mloc1 = fmaxf(mloc1, s0);
+        if (tl + 1 < lim1) mloc1 = fmaxf(mloc1, s1);
+        *reinterpret_cast<float2 *>(scores + r1 * SST + tl) = make_float2(s0, s1);
       }
     }
   }
 
-  // ---- softmax over the split's scores, per head: max, p = exp2(s - max) in place (0 past the
-  // context, up to the last tile's end), sum. With an empty context the sum is 0, so the output
-  // is NaN as in the reference. ----
-  mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 1));
-  mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 2));
-  if (row_ok && cq == 0) s_part[r0][warp] = mloc;
-  __syncthreads();
-  float m[G];
+  // ---- softmax over the split's scores, per row: max, p = exp2(s - max) in place (0 past the
+  // row's last visible key, up to the last tile's end), sum. A row that sees no key has sum 0,
+  // so its output is NaN as in the reference. ----
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    m[g] = s_part[g][0];
-#pragma unroll
-    for (int w = 1; w < kWarps; ++w) m[g] = fmaxf(m[g], s_part[g][w]);
+  for (int off = 1; off <= 2; off <<= 1) {
+    mloc0 = fmaxf(mloc0, __shfl_xor_sync(0xffffffffu, mloc0, off));
+    mloc1 = fmaxf(mloc1, __shfl_xor_sync(0xffffffffu, mloc1, off));
   }
-  if (tid < G) {
+  if (cq == 0) {
+    if (ok0) s_part[r0][warp] = mloc0;
+    if (ok1) s_part[r1][warp] = mloc1;
+  }
+  __syncthreads();
+  if (tid < R) {
     float mm = s_part[tid][0];
 #pragma unroll
     for (int w = 1; w < kWarps; ++w) mm = fmaxf(mm, s_part[tid][w]);
     s_m[tid] = mm;
   }
-  __syncthreads();  // s_part is reused for the sums
-  const int npad = nt * TT;
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
+  __syncthreads();
+  {
+    // TPR consecutive threads per row (all rows at once).
+    const int r = tid / TPR, sub = tid % TPR;
+    const int npad = nt * TT;
     float l = 0.f;
-    for (int i = tid; i < npad; i += kThreads) {
-      const float e = i < n ? exp2f(scores[g * p.chunk + i] - m[g]) : 0.f;
-      scores[g * p.chunk + i] = e;
-      l += e;
+    if (r < R) {
+      const float mr = s_m[r];
+      const int lim = s_lim[r];
+      float *row = scores + r * SST;
+      for (int i = sub; i < npad; i += TPR) {
+        const float e = i < lim ? exp2f(row[i] - mr) : 0.f;
+        row[i] = e;
+        l += e;
+      }
     }
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-    if (lane == 0) s_part[g][warp] = l;
-  }
-  __syncthreads();
-  if (tid < G) {
-    float l = 0.f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) l += s_part[tid][w];
-    s_l[tid] = l;
+    for (int off = TPR / 2; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+    if (r < R && sub == 0) s_l[r] = l;
   }
 
-  // ---- O[head][d] += P . V on the tensor cores; each warp owns D/4 output columns ----
+  // ---- O[row][d] += P . V on the tensor cores; each warp owns D/4 output columns ----
   float acc[PV_NT][4];
 #pragma unroll
   for (int q = 0; q < PV_NT; ++q)
@@ -622,63 +668,77 @@ __global__ void __launch_bounds__(kThreads, 4) paged_gqa_split_kernel(const Para
     __syncthreads();
     issue(j + kGqaStages - 1);
     const unsigned char *tile = ring + (j % kGqaStages) * kGqaTileBytes;
-    const float *prow = scores + r0 * p.chunk + (j - nt) * TT + 2 * cq;
+    const int tb = (j - nt) * TT + 2 * cq;
 #pragma unroll
     for (int ks = 0; ks < PV_KS; ++ks) {
-      uint32_t pa0 = 0u, pa2 = 0u;
-      if (row_ok) {
-        const float2 x = *reinterpret_cast<const float2 *>(prow + 16 * ks);
-        const float2 y = *reinterpret_cast<const float2 *>(prow + 16 * ks + 8);
+      uint32_t pa0 = 0u, pa1 = 0u, pa2 = 0u, pa3 = 0u;
+      if (ok0) {
+        const float *pr = scores + r0 * SST + tb + 16 * ks;
+        const float2 x = *reinterpret_cast<const float2 *>(pr);
+        const float2 y = *reinterpret_cast<const float2 *>(pr + 8);
         pa0 = Pack2<T>::pack(x.x, x.y);
         pa2 = Pack2<T>::pack(y.x, y.y);
+      }
+      if (ok1) {
+        const float *pr = scores + r1 * SST + tb + 16 * ks;
+        const float2 x = *reinterpret_cast<const float2 *>(pr);
+        const float2 y = *reinterpret_cast<const float2 *>(pr + 8);
+        pa1 = Pack2<T>::pack(x.x, x.y);
+        pa3 = Pack2<T>::pack(y.x, y.y);
       }
       const int row = 16 * ks + 8 * ((lane >> 3) & 1) + (lane & 7);
 #pragma unroll
       for (int np = 0; np < PV_NT / 2; ++np) {
         uint32_t bf[4];
         ldsm_x4_trans(bf, tile + tile_off<D>(row, warp * PV_NT + 2 * np + (lane >> 4)));
-        MmaRows8<T>::run(acc[2 * np], pa0, pa2, bf[0], bf[1]);
-        MmaRows8<T>::run(acc[2 * np + 1], pa0, pa2, bf[2], bf[3]);
+        Mma16816<T>::run(acc[2 * np], pa0, pa1, pa2, pa3, bf[0], bf[1]);
+        Mma16816<T>::run(acc[2 * np + 1], pa0, pa1, pa2, pa3, bf[2], bf[3]);
       }
     }
   }
   cp_async_wait<0>();
   __syncthreads();  // s_l is visible (also with no tiles)
 
-  if (row_ok) {
-    const int h = hk * G + r0;
-    const float inv_l = 1.f / s_l[r0];
-    const int64_t slot = (static_cast<int64_t>(b) * p.H + h) * p.num_splits + split;
+#pragma unroll
+  for (int half = 0; half < (kR16 ? 2 : 1); ++half) {
+    const int r = half ? r1 : r0;
+    if (half ? !ok1 : !ok0) continue;
+    const int g = r / p.Sq, s = r % p.Sq;
+    const int h = hk * p.G + g;
+    const float inv_l = 1.f / s_l[r];
+    const int64_t slot = ((static_cast<int64_t>(b) * p.H + h) * p.Sq + s) * p.num_splits + split;
 #pragma unroll
     for (int q = 0; q < PV_NT; ++q) {
       const int d = (warp * PV_NT + q) * 8 + 2 * cq;
+      const float v0 = acc[q][2 * half], v1 = acc[q][2 * half + 1];
       if (p.num_splits == 1) {
-        T *op = static_cast<T *>(p.o) + b * p.so0 + h * p.so1;
-        op[d * p.so3] = from_f32<T>(acc[q][0] * inv_l);
-        op[(d + 1) * p.so3] = from_f32<T>(acc[q][1] * inv_l);
+        T *op = static_cast<T *>(p.o) + b * p.so0 + h * p.so1 + s * p.so2;
+        op[d * p.so3] = from_f32<T>(v0 * inv_l);
+        op[(d + 1) * p.so3] = from_f32<T>(v1 * inv_l);
       } else {
-        *reinterpret_cast<float2 *>(p.ws_acc + slot * D + d) = make_float2(acc[q][0], acc[q][1]);
+        *reinterpret_cast<float2 *>(p.ws_acc + slot * D + d) = make_float2(v0, v1);
       }
     }
     if (p.num_splits > 1 && warp == 0 && cq == 0) {
-      p.ws_ml[2 * slot] = s_m[r0];
-      p.ws_ml[2 * slot + 1] = s_l[r0];
+      p.ws_ml[2 * slot] = s_m[r];
+      p.ws_ml[2 * slot + 1] = s_l[r];
     }
   }
 }
 
-// Ring, scores of the G heads, and the K and V byte offsets of the split's blocks (block
+// Ring, scores of the R query rows, and the K and V byte offsets of the split's blocks (block
 // size >= 16) and of the rows of a block (block size <= 64).
-size_t gqa_smem_bytes(int64_t G, int64_t chunk) {
+size_t gqa_smem_bytes(int64_t R, int64_t chunk) {
+  const int64_t tpr = R > 8 ? 8 : 16;
   return static_cast<size_t>(kGqaStages) * kGqaTileBytes +
-         static_cast<size_t>(G * chunk) * sizeof(float) +
+         static_cast<size_t>(R * (chunk + tpr)) * sizeof(float) +
          static_cast<size_t>(2 * (chunk / 16) + 2 * 64) * sizeof(int64_t);
 }
 
-template <typename T, int D, int G>
+template <typename T, int D, bool kR16>
 int launch_gqa_typed(const Params &p, cudaStream_t st) {
-  const size_t smem = gqa_smem_bytes(G, p.chunk);
-  auto kern = paged_gqa_split_kernel<T, D, G>;
+  const size_t smem = gqa_smem_bytes(static_cast<int64_t>(p.G) * p.Sq, p.chunk);
+  auto kern = paged_gqa_split_kernel<T, D, kR16>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
@@ -694,21 +754,18 @@ int launch_gqa_typed(const Params &p, cudaStream_t st) {
 
 template <typename T, int D>
 int launch_gqa_d(const Params &p, cudaStream_t st) {
-  switch (p.G) {
-    case 2: return launch_gqa_typed<T, D, 2>(p, st);
-    case 4: return launch_gqa_typed<T, D, 4>(p, st);
-    default: return launch_gqa_typed<T, D, 8>(p, st);
-  }
+  if (p.G * p.Sq > 8) return launch_gqa_typed<T, D, true>(p, st);
+  return launch_gqa_typed<T, D, false>(p, st);
 }
 
 }  // namespace
 
-Plan plan_gqa(int64_t B, int64_t H, int64_t Hkv, int64_t D, int64_t block_size,
+Plan plan_gqa(int64_t B, int64_t H, int64_t Hkv, int64_t Sq, int64_t D, int64_t block_size,
               int64_t max_blocks, int sms) {
   Plan pl = plan(B, Hkv, D, block_size, max_blocks, sms);
   if (pl.num_splits > 1) {
-    pl.ws_ml_floats = B * H * pl.num_splits * 2;
-    pl.ws_acc_floats = B * H * pl.num_splits * D;
+    pl.ws_ml_floats = B * H * Sq * pl.num_splits * 2;
+    pl.ws_acc_floats = B * H * Sq * pl.num_splits * D;
   }
   const size_t ml_bytes = ((pl.ws_ml_floats * sizeof(float)) + 255) / 256 * 256;
   pl.ws_bytes = ml_bytes + pl.ws_acc_floats * sizeof(float);
@@ -716,9 +773,9 @@ Plan plan_gqa(int64_t B, int64_t H, int64_t Hkv, int64_t D, int64_t block_size,
   return pl;
 }
 
-bool gqa_supported(int64_t G, int64_t D, const Plan &pl) {
-  return (G == 2 || G == 4 || G == 8) && (D == 64 || D == 128) &&
-         gqa_smem_bytes(G, pl.chunk) <= 200 * 1024;
+bool gqa_supported(int64_t G, int64_t Sq, int64_t D, const Plan &pl) {
+  return G >= 1 && Sq >= 1 && G * Sq <= 16 && (D == 64 || D == 128) &&
+         gqa_smem_bytes(G * Sq, pl.chunk) <= 200 * 1024;
 }
 
 int run_gqa(const Params &p, int dtype, cudaStream_t st) {

@@ -33,6 +33,12 @@ struct Params {
   // caches' head index is the KV head, q / o / the workspace use the H = G * Hkv query heads.
   int G = 1;
   int64_t Hkv = 0;
+  // Sq new tokens per sequence (q [B, H, Sq, D] with token stride sq2, o likewise with so2);
+  // with causal set, new token s sits at position len - Sq + s and sees the keys up to it.
+  // The workspace and the merge then index rows (b, h, s). The single-token entries keep 1.
+  int Sq = 1;
+  int causal = 0;
+  int64_t sq2 = 0, so2 = 0;
 };
 
 struct Plan {
@@ -57,13 +63,14 @@ int run(const Params &p, int dtype, cudaStream_t st);
 // Enqueues the merge of the split partials into o for the p.H heads.
 int run_merge(const Params &p, int dtype, cudaStream_t st);
 
-// Single-token decode with G = H / Hkv query heads per KV head on the CUDA cores: each token's
-// K and V rows are read once for all G heads. The plan is made over the KV heads; its
-// workspace holds the partials of all H query heads.
-Plan plan_gqa(int64_t B, int64_t H, int64_t Hkv, int64_t D, int64_t block_size,
+// Decode of Sq new tokens with G = H / Hkv query heads per KV head, G * Sq <= 16 query rows
+// per KV head: each token's K and V rows are read once for all rows. The plan is made over
+// the KV heads; its workspace holds the partials of all H * Sq query rows.
+Plan plan_gqa(int64_t B, int64_t H, int64_t Hkv, int64_t Sq, int64_t D, int64_t block_size,
               int64_t max_blocks, int sms);
-// Whether run_gqa handles this group size, head dim and plan (otherwise use another path).
-bool gqa_supported(int64_t G, int64_t D, const Plan &pl);
+// Whether run_gqa handles this group size, token count, head dim and plan (otherwise use
+// another path).
+bool gqa_supported(int64_t G, int64_t Sq, int64_t D, const Plan &pl);
 int run_gqa(const Params &p, int dtype, cudaStream_t st);
 
 }  // namespace paged

@@ -653,13 +653,15 @@ bool use_decode_path(int64_t Hq, int64_t Hkv, int64_t Sq, int64_t D) {
   (void)D;
   return Sq == 1 && Hq == Hkv;
 }
-// Single-token decode with 2, 4 or 8 query heads per KV head (D 64 or 128) goes to the
-// CUDA-core grouped-query split kernel, which reads each token's K/V rows once for the group.
+// Calls with at most 16 query rows per KV head (G = Hq / Hkv heads times Sq new tokens; D 64
+// or 128), other than the single-token Hq = Hkv case above, go to the grouped-query split
+// kernel, which reads each token's K/V rows once for all those rows.
 bool use_gqa_decode_path(int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t D,
                          int64_t block_size, int64_t max_blocks) {
-  if (Sq != 1 || Hq == Hkv) return false;
-  const paged::Plan pl = paged::plan_gqa(B, Hq, Hkv, D, block_size, max_blocks, sm_count());
-  return paged::gqa_supported(Hq / Hkv, D, pl);
+  if (Sq == 1 && Hq == Hkv) return false;
+  if ((Hq / Hkv) * Sq > 16) return false;
+  const paged::Plan pl = paged::plan_gqa(B, Hq, Hkv, Sq, D, block_size, max_blocks, sm_count());
+  return paged::gqa_supported(Hq / Hkv, Sq, D, pl);
 }
 }  // namespace
 }  // namespace ppf
@@ -674,7 +676,7 @@ extern "C" size_t tllm_paged_prefill_workspace_size(int64_t B, int64_t Hq, int64
   if (tllm::ppf::use_decode_path(Hq, Hkv, Sq, D))
     return tllm::paged::plan(B, Hq, D, block_size, max_blocks, tllm::sm_count()).ws_bytes;
   if (tllm::ppf::use_gqa_decode_path(B, Hq, Hkv, Sq, D, block_size, max_blocks))
-    return tllm::paged::plan_gqa(B, Hq, Hkv, D, block_size, max_blocks, tllm::sm_count()).ws_bytes;
+    return tllm::paged::plan_gqa(B, Hq, Hkv, Sq, D, block_size, max_blocks, tllm::sm_count()).ws_bytes;
   return tllm::ppf::make_plan(B, Hq, Hkv, Sq, D, block_size, max_blocks, tllm::sm_count()).ws_bytes;
 }
 
@@ -715,7 +717,7 @@ extern "C" int tllm_paged_prefill(const void *q, const void *k_cache, const void
                  "paged_prefill: q and the caches must be 16-byte aligned");
   const bool gqa = use_gqa_decode_path(B, Hq, Hkv, Sq, D, block_size, max_blocks);
   if (use_decode_path(Hq, Hkv, Sq, D) || gqa) {
-    const paged::Plan dp = gqa ? paged::plan_gqa(B, Hq, Hkv, D, block_size, max_blocks, sm_count())
+    const paged::Plan dp = gqa ? paged::plan_gqa(B, Hq, Hkv, Sq, D, block_size, max_blocks, sm_count())
                                : paged::plan(B, Hq, D, block_size, max_blocks, sm_count());
     paged::Params p{};
     p.q = q; p.k_cache = k_cache; p.v_cache = v_cache;
@@ -735,6 +737,10 @@ extern "C" int tllm_paged_prefill(const void *q, const void *k_cache, const void
     p.sm_scale = sm_scale;
     p.G = static_cast<int>(Hq / Hkv);
     p.Hkv = Hkv;
+    p.Sq = static_cast<int>(Sq);
+    p.causal = causal ? 1 : 0;
+    p.sq2 = sq[2];
+    p.so2 = so[2];
     int rc = paged::validate(p);
     if (rc) return rc;
     if (dp.num_splits > 1) {
