@@ -4,9 +4,11 @@
 Headline workload (N=1): swiglu at the Llama-3-8B MLP shape, x [4096, 4096], w1/w3
 [4096, 14336] fp16 (seed 1), metric TFLOP/s = 4*M*N*K / time. With N GPUs (torchrun, one
 process per GPU) the same problem is column-sharded over N (each rank computes
-out[:, N/g slice]); the GEMM epilogue stores each tile into every rank's [M, N] output over
-NVLink (CUDA IPC peer buffers) and synchronises with the peers inside the kernel, or with
---comm nccl the slices are all-gathered (strong scaling). At N>1 every rank checks 256
+out[:, N/g slice]); the GEMM epilogue stores each tile once through an NVLink multicast
+address, so the NVSwitch writes it into every rank's [M, N] output (torch symmetric memory;
+without multicast: into each rank's output over NVLink, CUDA IPC peer buffers), and
+synchronises with the peers inside the kernel, or with --comm nccl the slices are
+all-gathered (strong scaling). At N>1 every rank checks 256
 sampled rows of its gathered output bit for bit against the single-GPU operator.
 
 Also on the line:
@@ -66,9 +68,12 @@ def parse():
                     help="N>1 with --comm nccl: row chunks whose all-gather overlaps the next GEMM")
     ap.add_argument("--e2e-chunks", type=int, default=8,
                     help="column blocks of the 1-GPU end-to-end host pipeline")
-    ap.add_argument("--comm", choices=["peers", "nccl"], default="peers",
-                    help="N>1: peers = the GEMM epilogue stores into every rank's output over "
-                         "NVLink; nccl = all_gather_into_tensor + permute")
+    ap.add_argument("--comm", choices=["auto", "multicast", "peers", "nccl"], default="peers",
+                    help="N>1: multicast = the GEMM epilogue stores each tile once through an "
+                         "NVLink multicast address (NVSwitch writes every rank's output); peers "
+                         "= it stores into every rank's output over NVLink; nccl = "
+                         "all_gather_into_tensor + permute; auto = multicast where the devices "
+                         "offer it, else peers")
     ap.add_argument("--op", choices=sorted(OP_CASES), default=None,
                     help="run only this operator case (steps+warmup launches) and print its timing")
     return ap.parse_args()
@@ -565,11 +570,31 @@ def run_op(args):
                       "unit": unit, "launches": args.steps + args.warmup}), flush=True)
 
 
+def resolve_comm(comm: str) -> str:
+    """'auto' -> 'multicast' where this GPU offers NVLink multicast, else 'peers'."""
+    if comm != "auto":
+        return comm
+    try:
+        import torch
+        from torch._C._distributed_c10d import _SymmetricMemory
+
+        if torch.cuda.is_available() and _SymmetricMemory.has_multicast_support(
+                torch._C._autograd.DeviceType.CUDA, int(os.environ.get("LOCAL_RANK", "0"))):
+            return "multicast"
+    except Exception:  # no symmetric-memory support in this build: plain peer stores
+        pass
+    return "peers"
+
+
 def headline_config(world: int, comm: str, chunks: int) -> dict:
     """The headline workload's config, shared by both arms so the driver sees one config."""
     M, K, N = SWIGLU_SHAPE
     return {"workload": f"swiglu M{M} K{K} N{N} fp16 (Llama-3-8B MLP)",
             "parallelism": "single GPU" if world == 1 else (
+                f"column-shard N over {world} ranks; GEMM epilogue stores every tile once "
+                f"through an NVLink multicast address (NVSwitch writes all ranks' [M, N] "
+                f"outputs), peer handshake inside the kernel"
+                if comm == "multicast" else
                 f"column-shard N over {world} ranks; GEMM epilogue stores every tile into all "
                 f"ranks' [M, N] outputs over NVLink (CUDA IPC), peer handshake inside the kernel"
                 if comm == "peers" else
@@ -924,7 +949,8 @@ def _timed_ranks(torch, dist, world, fn, steps, warmup, flush=None):
     return _max_over_ranks(torch, dist, world, ms)
 
 
-def sharded_cfg5(torch, dist, T, S, world, rank, local, peaks, peak_src, with_cpu):
+def sharded_cfg5(torch, dist, T, S, world, rank, local, peaks, peak_src, with_cpu,
+                 multicast=False):
     """The Llama-3-70B-shaped sharded workloads at this world size (every rank)."""
     res = {}
     # These kernels run for milliseconds back to back: the sustained (power-capped) peak.
@@ -947,7 +973,7 @@ def sharded_cfg5(torch, dist, T, S, world, rank, local, peaks, peak_src, with_cp
     torch.cuda.empty_cache()
     peers = None
     if world > 1:
-        peers = S.PeerBuffers((M, N), torch.float16, dev)
+        peers = S.PeerBuffers((M, N), torch.float16, dev, multicast=multicast)
         step = lambda: S.swiglu_column_sharded(x, w1l, w3l, peers=peers)  # noqa: E731
     else:
         step = lambda: T.swiglu(x, w1l, w3l)  # noqa: E731
@@ -958,7 +984,9 @@ def sharded_cfg5(torch, dist, T, S, world, rank, local, peaks, peak_src, with_cp
     flops = 4.0 * M * K * N
     tf = flops / (ms * 1e-3) / 1e12
     t_tc = 4.0 * M * K * n_loc / (tc * 1e12)
-    t_link = (world - 1) * M * n_loc * 2 / (NVLINK_GBS * 1e9) if world > 1 else 0.0
+    # bytes a rank sends: its slice once through the multicast address, else once per peer
+    sent = (1 if multicast else world - 1) * M * n_loc * 2 if world > 1 else 0
+    t_link = sent / (NVLINK_GBS * 1e9)
     ent = {"value": tf, "unit": "TFLOP/s", "ms": ms, "flops": flops,
            "per_rank": f"x [{M}, {K}] and w1/w3 column slices [{K}, {n_loc}]; every rank ends "
                        f"with the whole [{M}, {N}] output",
@@ -970,7 +998,7 @@ def sharded_cfg5(torch, dist, T, S, world, rank, local, peaks, peak_src, with_cp
                         "note": f"slower of local FLOPs / {peak_src} sustained bf16 peak {tc:.0f} TFLOP/s and "
                                 f"bytes sent per rank / {NVLINK_GBS:.0f} GB/s peer-copy rate"}}
     if world > 1:
-        ent["nvlink_gbs_per_rank"] = (world - 1) * M * n_loc * 2 / (ms * 1e-3) / 1e9
+        ent["nvlink_gbs_per_rank"] = sent / (ms * 1e-3) / 1e9
     if with_cpu:
         ent["cpu_baseline"] = cpu_swiglu_baseline(cpu_swiglu_inputs(256, CFG5_SWIGLU, cols=4096, seed=4),
                                                   min_seconds=3.0, rows=256, shape=CFG5_SWIGLU)
@@ -1101,8 +1129,9 @@ def run_ours(args):
     out_full = None
     peers = None
     if world > 1:
-        if args.comm == "peers":
-            peers = S.PeerBuffers((M, N), torch.float16, torch.device("cuda", local))
+        if args.comm in ("peers", "multicast"):
+            peers = S.PeerBuffers((M, N), torch.float16, torch.device("cuda", local),
+                                  multicast=args.comm == "multicast")
         else:
             out_full = torch.empty((M, N), dtype=torch.float16, device="cuda")
 
@@ -1155,16 +1184,20 @@ def run_ours(args):
     else:
         k_ms = t_step
         t_tc = 4.0 * M * K * n_loc / (peak * 1e12)
-        sent = (world - 1) * M * n_loc * 2
+        mc = args.comm == "multicast"
+        # bytes this rank sends over NVLink per step: its slice once (multicast) or per peer
+        sent = (1 if mc else world - 1) * M * n_loc * 2
         t_link = sent / (NVLINK_GBS * 1e9)
+        kname = ("swiglu_pair_kernel<peers> (GEMM + output stored once through an NVLink multicast "
+                 "address)" if mc else
+                 "swiglu_pair_kernel<peers> (GEMM + output all-gather over NVLink)")
         if t_tc >= t_link:
             roofline = _roofline(4.0 * M * K * n_loc / (k_ms * 1e-3) / 1e12, peak, "TFLOP/s", "tensor",
-                                 f"{peak_src} bf16_tflops (dense, burst)", None,
-                                 "swiglu_pair_kernel<peers> (GEMM + output all-gather over NVLink)")
+                                 f"{peak_src} bf16_tflops (dense, burst)", None, kname)
         else:
             roofline = _roofline(sent / (k_ms * 1e-3) / 1e9, NVLINK_GBS, "GB/s", "nvlink",
                                  "measured NVLink peer-copy rate per direction on this pool", None,
-                                 "swiglu_pair_kernel<peers> (GEMM + output all-gather over NVLink)")
+                                 kname)
         roofline.update(kernel_ms=k_ms, tensor_ms=t_tc * 1e3, nvlink_ms=t_link * 1e3,
                         bytes_sent_per_rank=sent,
                         local_tflops=4.0 * M * K * n_loc / (k_ms * 1e-3) / 1e12,
@@ -1172,12 +1205,13 @@ def run_ours(args):
                              "bf16 peak and bytes sent per rank / NVLink rate")
         traffic = profile_traffic(f"swiglu_pair_kernel_peers_m4096_k4096_n14336_g{world}.md")
         roofline["traffic"] = traffic
-        # The one-CTA column-sharded kernel (128 x 128 tiles, half a CTA pair's tile time, so
-        # the first stores leave earlier) on the same step, for comparison.
-        ms1 = _max_over_ranks(torch, dist, world, _median_ms(
-            torch, lambda: S.swiglu_column_sharded(x, w1l, w3l, peers=peers, variant=1),
-            max(5, args.steps // 2), 2, flush))
-        roofline["one_cta_kernel_ms"] = ms1
+        if not mc:
+            # The one-CTA column-sharded kernel (128 x 128 tiles, half a CTA pair's tile time, so
+            # the first stores leave earlier) on the same step, for comparison.
+            ms1 = _max_over_ranks(torch, dist, world, _median_ms(
+                torch, lambda: S.swiglu_column_sharded(x, w1l, w3l, peers=peers, variant=1),
+                max(5, args.steps // 2), 2, flush))
+            roofline["one_cta_kernel_ms"] = ms1
 
     # End to end through the public API with pinned host buffers (H2D inputs, D2H result).
     hx = x.cpu().pin_memory()
@@ -1237,7 +1271,8 @@ def run_ours(args):
     cfg5 = None
     if not args.no_cfg5:
         cfg5 = sharded_cfg5(torch, dist, T, S, world, rank, local, peaks, peak_src,
-                            with_cpu=(rank == 0 and world == 1 and not args.no_cpu))
+                            with_cpu=(rank == 0 and world == 1 and not args.no_cpu),
+                            multicast=args.comm == "multicast")
 
     if rank == 0:
         line = {
@@ -1275,6 +1310,7 @@ def run_ours(args):
 
 def main():
     args = parse()
+    args.comm = resolve_comm(args.comm)
     if args.op is not None:
         run_op(args)
     elif args.impl == "reference":

@@ -222,6 +222,24 @@ TLLM_API int tllm_swiglu_colshard_peers(const void *x, const void *w1, const voi
                                         int64_t ldb3, int64_t ldo, int dtype, int variant,
                                         void *stream);
 
+/*
+ * tllm_swiglu_colshard_peers with the output written through an NVLink multicast address
+ * (no counterpart in the reference, which is single-GPU): mc is the multicast address of the
+ * outputs dsts[0..ndst), i.e. the same byte offsets of every rank's buffer bound to one
+ * multicast object (for example torch symmetric memory's multicast_ptr). The CTA-pair kernel
+ * (M >= 256, N % 128 == 0) then stores each output block once and the NVSwitch writes it into
+ * every rank's buffer, so a rank's NVLink egress is its own [M, N] slice instead of ndst - 1
+ * copies of it; other shapes run the one-CTA kernel, which stores into each of dsts as
+ * tllm_swiglu_colshard_peers does. flags, done, epoch and the handshake as there; the kernel
+ * choice is automatic. mc 16-byte aligned.
+ */
+TLLM_API int tllm_swiglu_colshard_multicast(const void *x, const void *w1, const void *w3,
+                                            void *const *dsts, void *mc,
+                                            uint32_t *const *flags, int ndst, int rank,
+                                            uint32_t *done, uint32_t epoch, int64_t M, int64_t N,
+                                            int64_t K, int64_t lda, int64_t ldb1, int64_t ldb3,
+                                            int64_t ldo, int dtype, void *stream);
+
 /* CUDA IPC set-up helpers for tllm_swiglu_colshard's peer buffers: a 64-byte handle and
  * byte offset for a device pointer, opening a peer's handle in this process, and closing it.
  * Not on the hot path. */

@@ -7,6 +7,8 @@ Per world size, one group of processes runs every mode:
   stores), one and two output slots,
   a column slice that is not a multiple of 128 (one-CTA kernel), several calls in a row with
   the output poisoned in between -- bit-identical to ``swiglu`` on one GPU;
+* swiglu column-sharded with the output stored once through an NVLink multicast address
+  (torch symmetric memory), where the devices offer multicast -- bit-identical;
 * swiglu column-sharded with the NCCL all-gather (1 and 2 row chunks) -- bit-identical;
 * flash_attention head-sharded -- bit-identical to the full problem's heads;
 * paged_attention batch-sharded over a token-balanced partition with rank-local block pools
@@ -30,6 +32,13 @@ def _port():
     p = s.getsockname()[1]
     s.close()
     return p
+
+
+def _multicast_ok():
+    from torch._C._distributed_c10d import _SymmetricMemory
+
+    return bool(_SymmetricMemory.has_multicast_support(torch._C._autograd.DeviceType.CUDA,
+                                                       torch.cuda.current_device()))
 
 
 def _swiglu_modes(rank, world, T, S, dist):
@@ -66,6 +75,28 @@ def _swiglu_modes(rank, world, T, S, dist):
                 dist.barrier()
                 peers.close()
                 res[f"peers m{m} nloc{n_loc} slots{slots} variant{variant}"] = ok
+        if _multicast_ok():
+            # Output stored once through an NVLink multicast address (CTA-pair kernel; the
+            # 136-column slice runs the one-CTA kernel with per-destination stores).
+            for slots in (1, 2):
+                peers = S.PeerBuffers((m, n), x.dtype, x.device, slots=slots, multicast=True)
+                ok = True
+                for _ in range(3):
+                    peers.local.fill_(float("nan"))
+                    torch.cuda.synchronize()
+                    dist.barrier()
+                    out = S.swiglu_column_sharded(x, w1l, w3l, peers=peers)
+                    torch.cuda.synchronize()
+                    ok = ok and bool(torch.equal(out, full))
+                outs = []
+                for _ in range(4):
+                    out = S.swiglu_column_sharded(x, w1l, w3l, peers=peers)
+                    outs.append(out.clone())
+                torch.cuda.synchronize()
+                ok = ok and all(bool(torch.equal(o, full)) for o in outs)
+                dist.barrier()
+                peers.close()
+                res[f"multicast m{m} nloc{n_loc} slots{slots}"] = ok
         for chunks in (1, 2):
             out = S.swiglu_column_sharded(x, w1l, w3l, chunks=chunks)
             torch.cuda.synchronize()

@@ -63,6 +63,12 @@ SIGNATURES = {
          ctypes.c_int, ctypes.c_int, _vp, ctypes.c_uint32, _i64, _i64, _i64, _i64, _i64, _i64,
          _i64, ctypes.c_int, ctypes.c_int, _vp],
     ),
+    "tllm_swiglu_colshard_multicast": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, ctypes.POINTER(ctypes.c_void_p), _vp, ctypes.POINTER(ctypes.c_void_p),
+         ctypes.c_int, ctypes.c_int, _vp, ctypes.c_uint32, _i64, _i64, _i64, _i64, _i64, _i64,
+         _i64, ctypes.c_int, _vp],
+    ),
     "tllm_ipc_get_handle": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(ctypes.c_uint64)]),
     "tllm_ipc_open": (ctypes.c_int, [_vp, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p),
                                      ctypes.POINTER(ctypes.c_void_p)]),

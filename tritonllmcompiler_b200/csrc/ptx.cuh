@@ -106,6 +106,15 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
   return v;
 }
 
+// 16-byte store through an NVLink multicast address: the switch writes it into the same offset
+// of every GPU's buffer bound to the multicast object (relaxed, system scope; order it before a
+// flag with a system-scope fence).
+__device__ __forceinline__ void multimem_st_v4(void *mc_addr, const uint4 &v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc_addr),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
 // ------------------------------------ TMA ----------------------------------------------
 // Tensor store of one 2-D box from shared memory (tracked in the bulk async-group).
 __device__ __forceinline__ void tma_store_2d(const void *map, uint32_t src, int c0, int c1) {

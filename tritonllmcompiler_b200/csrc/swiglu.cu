@@ -101,6 +101,10 @@ struct Geom {
   // boxes of {64, 2, 32}, so every row of a box leaves as one 256-byte span (instead of two
   // 128-byte boxes per row block).
   int store3d;
+  // CTA-pair column-sharded kernel: multicast address of the [M, ldo] output bound on every
+  // rank (null: none). With it, each warp writes its staged block once through the multicast
+  // address instead of once per destination.
+  void *mc;
 };
 
 // Tensor maps of the destinations' column slices (column-sharded CTA-pair kernel): map d
@@ -680,7 +684,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
-      if (kPeers && lane == 0) {
+      if (kPeers && g.mc != nullptr && remote_ok) {
+        // The warp's 32 rows x 128 columns once through the multicast address; the switch
+        // writes them into every rank's buffer. A lane stores 16-byte unit uu of row r for
+        // idx = 32 k + lane = 16 r + uu, so each half-warp writes 256 contiguous bytes of a row.
+        const int y = m0 + quad * 32;
+        T *mrow0 = static_cast<T *>(g.mc) + g.col_off + n0;
+#pragma unroll 4
+        for (int k = 0; k < 16; ++k) {
+          const int idx = 32 * k + lane;
+          const int r = idx >> 4, uu = idx & 15;
+          if (y + r < g.M) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(
+                wst + (uu >> 3) * 4096 + r * 128 + (((uu & 7) ^ (r & 7)) << 4));
+            multimem_st_v4(mrow0 + static_cast<int64_t>(y + r) * g.ldo + uu * 8, v);
+          }
+        }
+      } else if (kPeers && lane == 0) {
         // The warp's 32 rows x 128 columns into every destination's slice; rows past M are
         // clipped by the tensor maps.
         const int y = m0 + quad * 32;
@@ -710,6 +730,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       fence_proxy_async_global();
       __threadfence_system();
     }
+    // Multicast stores: every storing thread orders its stores before the flags that the
+    // last CTA raises after the barrier below.
+    if (kPeers && g.mc != nullptr) __threadfence_system();
   }
 
   tc_fence_before();
@@ -772,6 +795,7 @@ struct PeerArgs {
   int rank = 0;
   uint32_t *done = nullptr;
   uint32_t epoch = 0;
+  void *mc = nullptr;  // multicast address of the outputs (CTA-pair kernel only)
 };
 
 template <typename T>
@@ -851,6 +875,7 @@ int launch(const void *x, const void *w1, const void *w3, void *out, int64_t M, 
   g.done = pa.done;
   g.epoch = pa.epoch;
   g.store3d = 0;
+  g.mc = nullptr;
   g.vec_store = (ldo % 8 == 0 && col_off % 8 == 0 && dst_aligned &&
                  (ndst > 0 || aligned16(out))) ? 1 : 0;
   const int sms = sm_count();
@@ -872,6 +897,10 @@ int launch(const void *x, const void *w1, const void *w3, void *out, int64_t M, 
     PeerMaps pm;
     memset(&pm, 0, sizeof(pm));
     gp.store3d = variant == kVariantCtaPair3D ? 1 : 0;
+    if (pa.mc != nullptr) {
+      gp.mc = pa.mc;
+      gp.store3d = 0;  // the multicast stores read the 2-D staging layout
+    }
     for (int d = 0; d < ndst; ++d) {
       int rc;
       if (gp.store3d) {
@@ -1002,22 +1031,23 @@ extern "C" int tllm_swiglu_colshard(const void *x, const void *w1, const void *w
   return swiglu::launch<__nv_bfloat16>(x, w1, w3, dsts[0], M, N, K, lda, ldb1, ldb3, ldo, st, pa);
 }
 
-extern "C" int tllm_swiglu_colshard_peers(const void *x, const void *w1, const void *w3,
-                                          void *const *dsts, uint32_t *const *flags, int ndst,
-                                          int rank, uint32_t *done, uint32_t epoch, int64_t M,
-                                          int64_t N, int64_t K, int64_t lda, int64_t ldb1,
-                                          int64_t ldb3, int64_t ldo, int dtype, int variant,
-                                          void *stream) {
-  using namespace tllm;
-  clear_error();
+namespace tllm {
+namespace swiglu {
+namespace {
+// Shared by the two peer-handshake entries: argument checks, then the launch (mc: the
+// multicast address of the outputs, or null).
+int colshard_peers(const void *x, const void *w1, const void *w3, void *const *dsts,
+                   uint32_t *const *flags, int ndst, int rank, uint32_t *done, uint32_t epoch,
+                   int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb1, int64_t ldb3,
+                   int64_t ldo, int dtype, int variant, void *mc, void *stream) {
   TLLM_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "swiglu column-sharded: negative dimension");
   TLLM_CHECK_ARG(dtype == TLLM_DTYPE_F16 || dtype == TLLM_DTYPE_BF16,
                  "swiglu column-sharded: unsupported dtype %d", dtype);
   TLLM_CHECK_ARG(variant >= 0 && variant <= 3, "swiglu column-sharded: unknown kernel variant %d",
                  variant);
-  TLLM_CHECK_ARG(dsts && flags && done && ndst >= 1 && ndst <= swiglu::kMaxDst,
+  TLLM_CHECK_ARG(dsts && flags && done && ndst >= 1 && ndst <= kMaxDst,
                  "swiglu column-sharded: 1..%d destinations, their flags and a done counter required",
-                 swiglu::kMaxDst);
+                 kMaxDst);
   TLLM_CHECK_ARG(rank >= 0 && rank < ndst, "swiglu column-sharded: rank %d outside 0..%d", rank,
                  ndst - 1);
   TLLM_CHECK_ARG(epoch != 0, "swiglu column-sharded: epoch 0 is the flags' initial value");
@@ -1033,7 +1063,7 @@ extern "C" int tllm_swiglu_colshard_peers(const void *x, const void *w1, const v
                  "swiglu column-sharded: M, N and K must be positive");
   TLLM_CHECK_ARG(lda >= K && ldb1 >= N && ldb3 >= N, "swiglu column-sharded: leading dimension too small");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  swiglu::PeerArgs pa;
+  PeerArgs pa;
   pa.dsts = dsts;
   pa.ndst = ndst;
   pa.col_off = col_off;
@@ -1041,9 +1071,38 @@ extern "C" int tllm_swiglu_colshard_peers(const void *x, const void *w1, const v
   pa.rank = rank;
   pa.done = done;
   pa.epoch = epoch;
+  pa.mc = mc;
   if (dtype == TLLM_DTYPE_F16)
-    return swiglu::launch<__half>(x, w1, w3, dsts[rank], M, N, K, lda, ldb1, ldb3, ldo, st, pa,
+    return launch<__half>(x, w1, w3, dsts[rank], M, N, K, lda, ldb1, ldb3, ldo, st, pa,
                                   variant);
-  return swiglu::launch<__nv_bfloat16>(x, w1, w3, dsts[rank], M, N, K, lda, ldb1, ldb3, ldo, st, pa,
+  return launch<__nv_bfloat16>(x, w1, w3, dsts[rank], M, N, K, lda, ldb1, ldb3, ldo, st, pa,
                                        variant);
+}
+}  // namespace
+}  // namespace swiglu
+}  // namespace tllm
+
+extern "C" int tllm_swiglu_colshard_peers(const void *x, const void *w1, const void *w3,
+                                          void *const *dsts, uint32_t *const *flags, int ndst,
+                                          int rank, uint32_t *done, uint32_t epoch, int64_t M,
+                                          int64_t N, int64_t K, int64_t lda, int64_t ldb1,
+                                          int64_t ldb3, int64_t ldo, int dtype, int variant,
+                                          void *stream) {
+  tllm::clear_error();
+  return tllm::swiglu::colshard_peers(x, w1, w3, dsts, flags, ndst, rank, done, epoch, M, N, K, lda,
+                                      ldb1, ldb3, ldo, dtype, variant, nullptr, stream);
+}
+
+extern "C" int tllm_swiglu_colshard_multicast(const void *x, const void *w1, const void *w3,
+                                              void *const *dsts, void *mc,
+                                              uint32_t *const *flags, int ndst, int rank,
+                                              uint32_t *done, uint32_t epoch, int64_t M,
+                                              int64_t N, int64_t K, int64_t lda, int64_t ldb1,
+                                              int64_t ldb3, int64_t ldo, int dtype, void *stream) {
+  using namespace tllm;
+  clear_error();
+  TLLM_CHECK_ARG(mc != nullptr && (reinterpret_cast<uintptr_t>(mc) & 15u) == 0,
+                 "swiglu column-sharded: the multicast address must be non-null and 16-byte aligned");
+  return swiglu::colshard_peers(x, w1, w3, dsts, flags, ndst, rank, done, epoch, M, N, K, lda, ldb1,
+                                ldb3, ldo, dtype, 0, mc, stream);
 }

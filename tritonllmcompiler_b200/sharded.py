@@ -151,12 +151,18 @@ class PeerBuffers:
     landed, so a call's output is complete when its launch ends and stays valid until this
     rank's next call with the same slot (the call after next with two slots). Every rank
     must make every call. Create once per output shape (opening IPC handles is slow) and
-    ``close()`` before the process group goes away.
+    ``close()`` on every rank before the process group goes away.
+
+    With ``multicast=True`` the output buffers are torch symmetric memory bound to an NVLink
+    multicast object (``mc[slot]`` is its address): the CTA-pair kernel then stores each
+    output block once and the NVSwitch writes it into every rank's buffer, so a rank sends its
+    own slice over NVLink once instead of once per peer. Raises if the devices offer no
+    multicast.
     """
 
     FLAG_WORDS = 16  # TLLM_SWIGLU_PEER_FLAG_WORDS
 
-    def __init__(self, shape, dtype, device, group=None, slots: int = 2):
+    def __init__(self, shape, dtype, device, group=None, slots: int = 2, multicast: bool = False):
         assert slots in (1, 2)
         self.group = group
         self.world = dist.get_world_size(group)
@@ -166,12 +172,32 @@ class PeerBuffers:
         self.calls = 0
         self.device = torch.device(device)
         self._handles: list[bytes] = []
+        self._symm: list = []
+        self.mc: list[int] = []
         with torch.cuda.device(self.device):
-            self.locals = [torch.empty(shape, dtype=dtype, device=self.device) for _ in range(slots)]
             self.flags = torch.zeros(self.FLAG_WORDS, dtype=torch.int32, device=self.device)
             self.done = torch.zeros(1, dtype=torch.int32, device=self.device)
+            if multicast:
+                import torch.distributed._symmetric_memory as symm
+
+                name = (group if group is not None else dist.group.WORLD).group_name
+                self.locals = []
+                self.ptrs: list[list[int]] = []
+                for _ in range(slots):
+                    t = symm.empty(shape, dtype=dtype, device=self.device)
+                    h = symm.rendezvous(t, name)
+                    if not h.multicast_ptr:
+                        raise RuntimeError("PeerBuffers: no NVLink multicast on these devices")
+                    self._symm.append(h)
+                    self.locals.append(t)
+                    self.ptrs.append([int(p) for p in h.buffer_ptrs])
+                    self.mc.append(int(h.multicast_ptr))
+            else:
+                self.locals = [torch.empty(shape, dtype=dtype, device=self.device)
+                               for _ in range(slots)]
             torch.cuda.synchronize()  # zeroed before any peer can write a flag
-        self.ptrs: list[list[int]] = [self._share(t) for t in self.locals]
+        if not multicast:
+            self.ptrs = [self._share(t) for t in self.locals]
         self._arrs = [(ctypes.c_void_p * self.world)(*p) for p in self.ptrs]
         self._flag_arr = (ctypes.c_void_p * self.world)(*self._share(self.flags))
 
@@ -203,7 +229,13 @@ class PeerBuffers:
         return self.locals[self.calls % self.slots]
 
     def close(self):
+        """Collective (every rank): releases the peers' mappings; multicast buffers are freed
+        once every rank's device work is done."""
         with torch.cuda.device(self.device):
+            if self._symm:
+                torch.cuda.synchronize()
+                dist.barrier(group=self.group)
+                self._symm, self.mc, self.locals, self.ptrs = [], [], [], []
             for h in self._handles:
                 _ipc_release(h)
         self._handles = []
@@ -220,6 +252,15 @@ def _swiglu_into_peers(x, w1_local, w3_local, peers: PeerBuffers, variant: int =
     assert x.stride(1) == 1 and w1_local.stride(1) == 1 and w3_local.stride(1) == 1
     epoch = peers.calls % 0xFFFFFFFF + 1  # 1 .. 2^32 - 1, then 1 again; never 0 (the initial flags)
     with torch.cuda.device(x.device):
+        if peers.mc:
+            assert variant == 0, "the multicast path picks its kernel itself"
+            _lib.check(_lib.load().tllm_swiglu_colshard_multicast(
+                x.data_ptr(), w1_local.data_ptr(), w3_local.data_ptr(), peers._arrs[slot],
+                peers.mc[slot], peers._flag_arr, peers.world, peers.rank, peers.done.data_ptr(),
+                epoch, m, n_loc, k, x.stride(0), w1_local.stride(0), w3_local.stride(0),
+                out.stride(0), _lib.DTYPE_CODES[x.dtype], _lib.stream_of(x)))
+            peers.calls += 1
+            return out
         _lib.check(_lib.load().tllm_swiglu_colshard_peers(
             x.data_ptr(), w1_local.data_ptr(), w3_local.data_ptr(), peers._arrs[slot],
             peers._flag_arr, peers.world, peers.rank, peers.done.data_ptr(), epoch, m, n_loc, k,
